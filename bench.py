@@ -1,0 +1,387 @@
+#!/usr/bin/env python3
+"""Benchmark of the paged-attention decode step (fused KV write + attention).
+
+Workload: the 22B-shaped decode of the benchmark configuration -- 32 query /
+8 KV heads, head_size 128, block_size 16, context lengths log-normal (median
+2048, sigma 0.6) clipped to [512, 8192] -- at batch 1024, sharded by sequence
+(greedy LPT on context length) across the N GPUs: total work is fixed, so
+scaling is "strong".  A step = one fused decode over the rank's shard, inputs
+resident in HBM (KV pool >> L2, so no L2 flush is needed).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  (N > 1: launched by torch.distributed.run, one rank per GPU, NCCL)
+
+value = aggregate algorithmic HBM GB/s over all ranks (bytes a perfect kernel
+must move per step / max-over-ranks step time); also reported: seq-tokens/s.
+e2e = the same metric through the engine op API (PagedAttentionOp
+.encode_decode_fused) with per-step H2D copies of q/new K/new V/block table/
+seq_lens from pinned host memory and a D2H copy of the output.
+--impl reference times the reference's own CPU path (restated in
+oracle/mps_port.py: scatter + per-sequence gather + GQA repeat + SDPA) on the
+host cores on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "vllm-apple_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+WORKLOAD = "devstral_b1024"
+METRIC = "paged-attn decode HBM GB/s (algorithmic bytes) at batch 1024, 22B shape"
+UNIT = "GB/s"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic(workload: str):
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", f"paged_decode_{workload}.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling while the timed region runs."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,utilization.gpu,"
+         "clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+        return False
+
+    def summary(self):
+        rows = []
+        for line in (self.out or "").strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 10:
+                continue
+            try:
+                rows.append(dict(sm=float(f[1]), smax=float(f[2]), util=float(f[4]),
+                                 hw=f[6], hwt=f[7], swt=f[8], pcap=f[9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        load = [r for r in rows if r["util"] > 0] or rows
+        reasons = set()
+        for r in load:
+            for k, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                            ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
+                if r[k].lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in load),
+                "sm_max_mhz": max(r["smax"] for r in rows), "reasons": sorted(reasons),
+                "samples": len(load)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus and world > 1:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    return world, rank, local
+
+
+def global_lengths():
+    from vllm_apple_b200.workloads import DECODE_CONFIGS, draw_lengths
+    c = DECODE_CONFIGS[WORKLOAD]
+    gen = torch.Generator().manual_seed(0)
+    return draw_lengths(c["dist"], c["batch"], gen)
+
+
+def run_ours(args, world, rank, local):
+    from vllm_apple_b200 import ops
+    from vllm_apple_b200.engine import EngineContext, PagedAttentionOp
+    from vllm_apple_b200.workloads import lpt_shard, make_decode_case
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+        pg = dist
+    L_all = global_lengths()
+    shards = lpt_shard(L_all.tolist(), world)
+    case = make_decode_case(WORKLOAD, device=dev, seed=0, seq_subset=shards[rank],
+                            lengths=L_all)
+    B = case.batch
+    q, nk, nv = case.q.to(dev), case.new_k.to(dev), case.new_v.to(dev)
+    bt, sl = case.block_table.to(dev), case.seq_lens.to(dev)
+    out = torch.empty_like(q)
+    max_len = case.max_seq_len
+    lib_ws = ops._lib.load().va_paged_decode_workspace_size(B, case.Hq, case.Hkv, case.D,
+                                                            case.bs, max_len)
+    launches_per_step = 2 if lib_ws else 1
+
+    def step():
+        ops.paged_decode(out, q, case.k_cache, case.v_cache, bt, sl, scale=case.scale,
+                         max_seq_len=max_len, new_k=nk, new_v=nv, layout="hnd")
+
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    ops.check_device_errors(local)
+
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        torch.cuda.synchronize(dev)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+    ms_local = t0.elapsed_time(t1)
+    ops.check_device_errors(local)
+
+    # ---- e2e through the engine op API with host buffers ----
+    ctx = EngineContext(local)
+    op = PagedAttentionOp(ctx, case.Hkv, case.Hq, case.D, case.bs, case.scale)
+    h_q, h_nk, h_nv = (t.pin_memory() for t in (case.q, case.new_k, case.new_v))
+    h_bt, h_sl = case.block_table.pin_memory(), case.seq_lens.pin_memory()
+    h_out = torch.empty(case.q.shape, dtype=torch.float16).pin_memory()
+    d_q, d_nk, d_nv = torch.empty_like(q), torch.empty_like(nk), torch.empty_like(nv)
+    d_bt, d_sl, d_out = torch.empty_like(bt), torch.empty_like(sl), torch.empty_like(out)
+    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_nk, h_nv, h_bt, h_sl))
+    d2h = h_out.numel() * h_out.element_size()
+
+    def e2e_step():
+        with ctx.new_step(step_kind="decode", num_seqs=B) as sc:
+            for d, h in ((d_q, h_q), (d_nk, h_nk), (d_nv, h_nv), (d_bt, h_bt), (d_sl, h_sl)):
+                d.copy_(h, non_blocking=True)
+            op.encode_decode_fused(sc, d_q, d_nk, d_nv, case.k_cache, case.v_cache, d_bt, d_sl,
+                                   d_out, B, max_len, max_blocks_per_seq=d_bt.shape[1])
+            h_out.copy_(d_out, non_blocking=True)
+
+    for _ in range(max(3, args.warmup // 4)):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    e2e_steps = max(1, min(args.steps, 50))
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms_local = e0.elapsed_time(e1) / e2e_steps
+    ops.check_device_errors(local)
+
+    # ---- aggregate over ranks ----
+    local_bytes = case.algorithmic_bytes()
+    local_tokens = case.context_tokens
+    vec = torch.tensor([ms_local / args.steps, e2e_ms_local], dtype=torch.float64, device=dev)
+    tot = torch.tensor([float(local_bytes), float(local_tokens)], dtype=torch.float64, device=dev)
+    if pg is not None:
+        pg.all_reduce(vec, op=pg.ReduceOp.MAX)
+        pg.all_reduce(tot, op=pg.ReduceOp.SUM)
+    ms_step, e2e_ms = vec.tolist()
+    all_bytes, all_tokens = tot.tolist()
+    if rank != 0:
+        if pg is not None:
+            pg.destroy_process_group()
+        return None
+
+    value = all_bytes / (ms_step * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+    # roofline of the dominant kernel on this rank (the step is that kernel plus a
+    # small split combine): algorithmic bytes per launch / mean step time
+    achieved = local_bytes / (ms_local / args.steps * 1e-3) / 1e9
+    traffic = ncu_traffic(WORKLOAD) if world == 1 else None
+    res = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic (seeded N(0,1) fp16 q/k/v, log-normal lengths)",
+        "config": {"workload": WORKLOAD + "_decode", "global_batch": 1024, "Hq": 32, "Hkv": 8,
+                   "head_size": 128, "block_size": 16, "ctx": "lognormal(2048,0.6) in [512,8192]",
+                   "context_tokens": int(all_tokens), "sharding": "LPT by context length",
+                   "layout": "engine [nb,Hkv,bs,D]",
+                   "l2": "inputs larger than L2 (no flush)", "parallelism": f"seq-shard x{world}"},
+        "seq_tokens_per_s": round(all_tokens / (ms_step * 1e-3), 1),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": traffic,
+                     "algorithmic_bytes_per_launch": int(local_bytes)},
+        "e2e": {"value": round(all_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": UNIT,
+                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h),
+                "api": "engine PagedAttentionOp.encode_decode_fused"},
+        "gpu_launches": args.steps * launches_per_step,
+        "clocks": clk.summary(),
+    }
+    if world == 1:
+        res["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
+    if pg is not None:
+        pg.destroy_process_group()
+    return res
+
+
+def cpu_sample_case(n_seqs: int):
+    from vllm_apple_b200.workloads import make_decode_case
+    L_all = global_lengths()
+    return make_decode_case(WORKLOAD, device="cpu", seed=0, layout="nhd",
+                            seq_subset=list(range(n_seqs)), lengths=L_all)
+
+
+def cpu_time_sample(case, reps_budget_s: float):
+    """Time the reference's CPU path (oracle/mps_port.py) on `case`; returns
+    (seconds per pass, passes)."""
+    from oracle import mps_port
+    kv = torch.stack([case.k_cache, case.v_cache])
+    B = case.batch
+    out = torch.empty_like(case.q)
+    slots = case.slot_mapping
+    qsl = list(range(B + 1))
+    bt = case.block_table.to(torch.int64)
+
+    def one():
+        mps_port.forward(case.q, case.new_k, case.new_v, kv, bt, case.seq_lens.tolist(), slots,
+                         qsl, B, case.scale, case.Hkv, out)
+
+    one()  # warm-up
+    times = []
+    t_end = time.perf_counter() + reps_budget_s
+    while True:
+        t = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t)
+        if time.perf_counter() > t_end or len(times) >= 5:
+            break
+    return min(times), len(times)
+
+
+def cpu_baseline(budget_s: float = 15.0, n_seqs: int = 48):
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    case = cpu_sample_case(n_seqs)
+    sec, n = cpu_time_sample(case, budget_s)
+    return {"value": round(case.algorithmic_bytes() / sec / 1e9, 3), "unit": UNIT,
+            "cores": threads, "kind": "port",
+            "sample": f"first {n_seqs} of the {WORKLOAD} sequences ({case.context_tokens} "
+                      f"context tokens), reference torch CPU path (oracle/mps_port.py, "
+                      f"vLLM layout), best of {n} passes",
+            "seq_tokens_per_s": round(case.context_tokens / sec, 1)}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    n_seqs = 48
+    case = cpu_sample_case(n_seqs)
+    from oracle import mps_port  # noqa: F401  (fail early if the oracle is missing)
+    for _ in range(args.warmup):
+        cpu_time_sample(case, 0.0)
+    times = []
+    for _ in range(args.steps):
+        s, _ = cpu_time_sample(case, 0.0)
+        times.append(s)
+    sec = statistics.median(times)
+    value = case.algorithmic_bytes() / sec / 1e9
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": WORKLOAD + "_decode", "global_batch": 1024,
+                   "sample_seqs": n_seqs, "context_tokens": case.context_tokens},
+        "seq_tokens_per_s": round(case.context_tokens / sec, 1),
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads,
+                         "kind": "port",
+                         "sample": f"first {n_seqs} of {WORKLOAD} sequences per step, "
+                                   "reference torch CPU path restated in oracle/mps_port.py"},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world, rank, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        res = run_reference(args, world, rank)
+    else:
+        res = run_ours(args, world, rank, local)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,95 @@
+"""Token-parallel causal paged attention (prefill / mixed batch) vs the oracle."""
+import numpy as np
+import pytest
+import torch
+
+from _util import ATOL, bits, max_abs, np16
+from oracle import paged_attention as ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from vllm_apple_b200 import ops
+    return ops
+
+
+def _run(c, token_to_seq=None, positions=None):
+    """Scatter all new K/V rows by slot, then prefill attention (engine order)."""
+    ops = _ops()
+    dk, dv = c.k_cache.cuda(), c.v_cache.cuda()
+    ops.kv_write_slots(dk, dv, c.k.cuda(), c.v.cuda(), c.slot_mapping.cuda(), c.layout)
+    q = c.q.cuda()
+    out = torch.full_like(q, 7.0)
+    ts = c.token_to_seq if token_to_seq is None else token_to_seq
+    ps = c.positions if positions is None else positions
+    ops.paged_prefill(out, q, dk, dv, c.block_table.cuda(), ts.cuda(), ps.cuda(),
+                      scale=c.scale, layout=c.layout)
+    torch.cuda.synchronize()
+    return out, dk, dv, ops.check_device_errors(raise_on_error=False)
+
+
+def _oracle(c, token_to_seq=None, positions=None):
+    rk, rv = c.k_cache.cpu().numpy().copy(), c.v_cache.cpu().numpy().copy()
+    ref.kv_write_slots_vectorized(rk, rv, c.k.numpy(), c.v.numpy(), c.slot_mapping.numpy(),
+                                  c.layout)
+    ts = c.token_to_seq if token_to_seq is None else token_to_seq
+    ps = c.positions if positions is None else positions
+    o = ref.paged_prefill(c.q.numpy(), rk, rv, c.block_table.numpy(), ts.numpy(), ps.numpy(),
+                          c.scale, layout=c.layout)
+    return o, rk, rv
+
+
+@pytest.mark.parametrize("layout", ["hnd", "nhd"])
+def test_mixed_batch_config4(layout):
+    """Config 4: 4 chunks of 512 tokens over prior context + 60 decode rows."""
+    from vllm_apple_b200.workloads import make_mixed_case
+    c = make_mixed_case(layout=layout, seed=0)
+    out, dk, dv, bad = _run(c)
+    assert bad == 0
+    o, rk, rv = _oracle(c)
+    err = max_abs(np16(out), o)
+    assert err <= ATOL, f"max abs err {err}"
+    np.testing.assert_array_equal(bits(dk), rk.view(np.int16))
+    np.testing.assert_array_equal(bits(dv), rv.view(np.int16))
+
+
+@pytest.mark.parametrize("Hq,Hkv,D", [(14, 2, 64), (8, 8, 128), (16, 2, 96), (8, 2, 32),
+                                      (64, 4, 128)])
+def test_prefill_shapes(Hq, Hkv, D):
+    from vllm_apple_b200.workloads import make_mixed_case
+    c = make_mixed_case(Hq=Hq, Hkv=Hkv, D=D, num_chunks=3, chunk=70, prior=(0, 300),
+                        num_decode=5, decode_len=(1, 400), seed=Hq + D)
+    out, _, _, bad = _run(c)
+    assert bad == 0
+    o, _, _ = _oracle(c)
+    assert max_abs(np16(out), o) <= ATOL
+
+
+def test_prefill_from_empty_cache_is_plain_causal_attention():
+    """No prior context: the engine semantics equal causal SDPA over the chunk."""
+    from vllm_apple_b200.workloads import make_mixed_case
+    c = make_mixed_case(num_chunks=2, chunk=100, prior=(0, 0), num_decode=0, seed=3)
+    out, _, _, _ = _run(c)
+    q = c.q.float().view(2, 100, 32, 128).transpose(1, 2)
+    k = c.k.float().view(2, 100, 8, 128).transpose(1, 2).repeat_interleave(4, dim=1)
+    v = c.v.float().view(2, 100, 8, 128).transpose(1, 2).repeat_interleave(4, dim=1)
+    exp = torch.nn.functional.scaled_dot_product_attention(q, k, v, is_causal=True,
+                                                           scale=c.scale)
+    exp = exp.transpose(1, 2).reshape(200, 32, 128)
+    assert max_abs(np16(out), exp.numpy()) <= ATOL
+
+
+def test_prefill_skips_invalid_tokens():
+    from vllm_apple_b200.workloads import make_mixed_case
+    c = make_mixed_case(num_chunks=1, chunk=40, prior=(10, 10), num_decode=3,
+                        decode_len=(20, 60), seed=4)
+    ts = c.token_to_seq.clone()
+    ps = c.positions.clone()
+    ts[1] = -1          # invalid sequence
+    ps[5] = -1          # negative position
+    out, _, _, _ = _run(c, ts, ps)
+    o, _, _ = _oracle(c, ts, ps)
+    assert torch.all(out[1].cpu() == 7.0) and torch.all(out[5].cpu() == 7.0)
+    keep = [i for i in range(c.num_tokens) if i not in (1, 5)]
+    assert max_abs(np16(out)[keep], o[keep]) <= ATOL

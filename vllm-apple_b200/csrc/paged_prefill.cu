@@ -1,0 +1,505 @@
+// Token-parallel causal paged attention (prefill / chunked-prefill mixed batch).
+//
+// Semantics of the reference's paged_attention_v2_prefill: token t of
+// sequence token_to_seq[t] attends to cache positions 0..positions[t].
+//
+// Design:
+//   * a one-CTA planner kernel cuts the token list into tiles: a tile is at
+//     most TQ consecutive tokens of one sequence (run boundaries found with a
+//     block-wide max-scan, tile slots with a sum-scan).  Decode rows of a mixed
+//     batch become one-token tiles.
+//   * one CTA (4 warps) per (tile, kv head [, q-head group]).  Its 64 MMA rows
+//     are (token, q head) pairs of the GQA group, so every K/V tile staged in
+//     shared memory serves all heads of the group.
+//   * K/V move HBM -> shared memory in chunks of 64 keys (4 pages) with
+//     16-byte cp.async into padded rows (conflict-free ldmatrix), double
+//     buffered; unwritten positions and invalid pages are zero-filled.
+//   * S = Q K^T and O += P V on tensor cores (mma.sync m16n8k16, fp16 in, fp32
+//     accumulate), online softmax in registers, per-row causal mask by
+//     absolute position.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int kRows = 64;   // MMA rows per CTA (4 warps x 16)
+constexpr int kKeys = 64;   // keys per staged chunk (4 pages of 16)
+constexpr int kThreads = 128;
+
+// ---------------------------------------------------------------------------
+// planner: tiles[i] = {first token, token count}; tiles_n = number of tiles
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) plan_tiles_kernel(const int32_t *token_to_seq,
+                                                          int64_t T, int TQ, int2 *tiles,
+                                                          int32_t *tiles_n, int64_t max_tiles,
+                                                          int32_t *err) {
+  __shared__ int warp_buf[32];
+  __shared__ int carry_max, carry_sum;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  if (tid == 0) { carry_max = 0; carry_sum = 0; }
+  __syncthreads();
+  for (int64_t base = 0; base < T; base += 1024) {
+    const int64_t t = base + tid;
+    const bool in = t < T;
+    const int s = in ? token_to_seq[t] : 0;
+    const bool run_start = in && (t == 0 || token_to_seq[t - 1] != s);
+    // inclusive max-scan of run starts
+    int v = run_start ? (int)t : -1;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v = max(v, n);
+    }
+    if (lane == 31) warp_buf[wid] = v;
+    __syncthreads();
+    if (wid == 0) {
+      int w = warp_buf[lane];
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w = max(w, n);
+      }
+      warp_buf[lane] = w;
+    }
+    __syncthreads();
+    int rs = v;
+    if (wid > 0) rs = max(rs, warp_buf[wid - 1]);
+    rs = max(rs, carry_max);
+    const bool tstart = in && ((t - rs) % TQ == 0);
+    __syncthreads();
+    if (tid == 1023) carry_max = rs;
+    // exclusive sum-scan of tile starts
+    int c = tstart ? 1 : 0;
+    int x = c;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += n;
+    }
+    if (lane == 31) warp_buf[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+      int w = warp_buf[lane];
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += n;
+      }
+      warp_buf[lane] = w;
+    }
+    __syncthreads();
+    const int excl = x - c + (wid > 0 ? warp_buf[wid - 1] : 0) + carry_sum;
+    if (tstart) {
+      if (excl < max_tiles) tiles[excl] = make_int2((int)t, 0);
+      else va::raise_flag(err, VA_FLAG_CTX_OVERFLOW);
+    }
+    __syncthreads();
+    if (tid == 1023) carry_sum = excl + c;
+    __syncthreads();
+  }
+  __syncthreads();
+  const int n = carry_sum < max_tiles ? carry_sum : (int)max_tiles;
+  for (int i = tid; i < n; i += 1024) {
+    const int next = (i + 1 < n) ? tiles[i + 1].x : (int)T;
+    tiles[i].y = next - tiles[i].x;
+  }
+  if (tid == 0) *tiles_n = n;
+}
+
+// ---------------------------------------------------------------------------
+// attention
+// ---------------------------------------------------------------------------
+struct PrefillArgs {
+  __half *out;
+  const __half *q, *kc, *vc;
+  const int32_t *bt, *tok_seq, *pos;
+  const int2 *tiles;
+  const int32_t *tiles_n;
+  int32_t *err;
+  int64_t num_seqs, max_blocks, num_blocks;
+  int Hq, Hkv, G, hgroups, TQ, bs;
+  float scale_log2;
+  int64_t s_block, s_head, s_token, q_s_token, q_s_head, o_s_token, o_s_head;
+};
+
+VA_DEVINL void cp_async16(void *smem, const void *g) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(va::smem_addr(smem)), "l"(g)
+               : "memory");
+}
+VA_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+VA_DEVINL void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+VA_DEVINL void ldsm_x4(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(va::smem_addr(p)));
+}
+VA_DEVINL void ldsm_x4_t(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3, const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(va::smem_addr(p)));
+}
+VA_DEVINL void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+VA_DEVINL uint32_t pack_h2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+template <int D>
+struct PShape {
+  static constexpr int CPR = D / 8;        // 16-byte chunks per row
+  static constexpr int LD = D + 8;         // padded row (halves): odd chunk count
+  static constexpr size_t kTile = size_t(kKeys) * LD;  // halves per K or V chunk tile
+  static constexpr size_t kSmem = (size_t(kRows) * LD + 4 * kTile) * 2;
+};
+
+template <int D, int GC>
+__global__ void __launch_bounds__(kThreads) paged_prefill_kernel(const PrefillArgs a) {
+  using S = PShape<D>;
+  constexpr int LD = S::LD, CPR = S::CPR;
+  extern __shared__ __align__(128) unsigned char smem[];
+  __half *Qs = reinterpret_cast<__half *>(smem);
+  __half *Ks = Qs + kRows * LD;       // [2][kKeys][LD]
+  __half *Vs = Ks + 2 * S::kTile;     // [2][kKeys][LD]
+  __shared__ int s_pos[kRows];        // per-token position (-1: token skipped)
+  __shared__ int s_ctx, s_bad_from;
+
+  const int tile = blockIdx.x;
+  if (tile >= *a.tiles_n) return;
+  const int2 td = a.tiles[tile];
+  const int t0 = td.x, nq = td.y;
+  const int seq = a.tok_seq[t0];
+  const int kvh = blockIdx.y / a.hgroups, hg = blockIdx.y - (blockIdx.y / a.hgroups) * a.hgroups;
+  const int head0 = kvh * a.G + hg * GC;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int BS = a.bs;
+
+  if (tid == 0) { s_ctx = 0; s_bad_from = INT_MAX; }
+  __syncthreads();
+  if (tid < a.TQ) {
+    int p = -1;
+    if (tid < nq && seq >= 0 && seq < a.num_seqs) {
+      p = a.pos[t0 + tid];
+      if (p >= 0 && (int64_t)((p + BS) / BS) > a.max_blocks) {
+        va::raise_flag(a.err, VA_FLAG_CTX_OVERFLOW);
+        p = -1;
+      }
+      if (p < 0) p = -1;
+    }
+    s_pos[tid] = p;
+    if (p >= 0) atomicMax(&s_ctx, p + 1);
+  }
+  __syncthreads();
+  const int ctx = s_ctx;
+  if (ctx == 0) return;
+  const int32_t *bt_row = a.bt + (int64_t)seq * a.max_blocks;
+  const int nchunks = (ctx + kKeys - 1) / kKeys;
+
+  // ---- stage Q rows (token-major, head-minor) ----
+  for (int i = tid; i < kRows * CPR; i += kThreads) {
+    const int r = i / CPR, c = i - r * CPR;
+    const int tk = r / GC, g = r - tk * GC;
+    __half *dst = Qs + r * LD + c * 8;
+    if (tk < nq && r < a.TQ * GC) {
+      cp_async16(dst, a.q + (int64_t)(t0 + tk) * a.q_s_token + (int64_t)(head0 + g) * a.q_s_head +
+                          c * 8);
+    } else {
+      *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+    }
+  }
+
+  auto load_chunk = [&](int ch, int buf) {
+    __half *kd = Ks + buf * S::kTile, *vd = Vs + buf * S::kTile;
+    for (int i = tid; i < kKeys * CPR; i += kThreads) {
+      const int r = i / CPR, c = i - r * CPR;
+      const int key = ch * kKeys + r;
+      const int page = key / BS, off = key - page * BS;
+      bool ok = key < ctx;
+      int32_t blk = -1;
+      if (ok) {
+        blk = bt_row[page];
+        if (blk < 0 || blk >= a.num_blocks) {
+          ok = false;
+          atomicMin(&s_bad_from, page * BS);
+        }
+      }
+      __half *kdst = kd + r * LD + c * 8, *vdst = vd + r * LD + c * 8;
+      if (ok) {
+        const int64_t src = (int64_t)blk * a.s_block + (int64_t)kvh * a.s_head +
+                            (int64_t)off * a.s_token + c * 8;
+        cp_async16(kdst, a.kc + src);
+        cp_async16(vdst, a.vc + src);
+      } else {
+        *reinterpret_cast<uint4 *>(kdst) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4 *>(vdst) = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+
+  load_chunk(0, 0);
+  cp_async_commit();
+
+  // per-lane row bookkeeping: rows r0 = warp*16 + lane/4 and r0 + 8
+  const int rA = warp * 16 + (lane >> 2), rB = rA + 8;
+  const int tkA = rA / GC, tkB = rB / GC;
+  const int posA = (rA < a.TQ * GC && tkA < a.TQ) ? s_pos[tkA] : -1;
+  const int posB = (rB < a.TQ * GC && tkB < a.TQ) ? s_pos[tkB] : -1;
+
+  uint32_t qf[D / 16][4];
+  float o[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float mA = -INFINITY, mB = -INFINITY, lA = 0.f, lB = 0.f;
+
+#pragma unroll 1
+  for (int ch = 0; ch < nchunks; ++ch) {
+    const int buf = ch & 1;
+    if (ch + 1 < nchunks) {
+      load_chunk(ch + 1, buf ^ 1);
+      cp_async_commit();
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    if (ch == 0) {  // Q fragments (A operand), kept in registers for the whole loop
+      const int lr = warp * 16 + (lane & 15), lc = (lane >> 4) * 8;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk)
+        ldsm_x4(qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], Qs + lr * LD + kk * 16 + lc);
+    }
+    const __half *kt = Ks + buf * S::kTile, *vt = Vs + buf * S::kTile;
+    // ---- S = Q K^T (16 rows x 64 keys per warp) ----
+    float s[kKeys / 8][4];
+#pragma unroll
+    for (int n = 0; n < kKeys / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+      for (int n = 0; n < kKeys / 8; n += 2) {
+        // matrices: (n, k lo), (n, k hi), (n+1, k lo), (n+1, k hi)
+        const int key = n * 8 + (lane & 7) + ((lane >> 4) << 3);
+        const int col = kk * 16 + ((lane >> 3) & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(b0, b1, b2, b3, kt + key * LD + col);
+        mma16816(s[n], qf[kk], b0, b1);
+        mma16816(s[n + 1], qf[kk], b2, b3);
+      }
+    }
+    // ---- mask + online softmax ----
+    float mxA = -INFINITY, mxB = -INFINITY;
+#pragma unroll
+    for (int n = 0; n < kKeys / 8; ++n) {
+      const int j = ch * kKeys + n * 8 + 2 * (lane & 3);
+      s[n][0] = (j <= posA) ? s[n][0] * a.scale_log2 : -INFINITY;
+      s[n][1] = (j + 1 <= posA) ? s[n][1] * a.scale_log2 : -INFINITY;
+      s[n][2] = (j <= posB) ? s[n][2] * a.scale_log2 : -INFINITY;
+      s[n][3] = (j + 1 <= posB) ? s[n][3] * a.scale_log2 : -INFINITY;
+      mxA = fmaxf(mxA, fmaxf(s[n][0], s[n][1]));
+      mxB = fmaxf(mxB, fmaxf(s[n][2], s[n][3]));
+    }
+#pragma unroll
+    for (int o2 = 1; o2 < 4; o2 <<= 1) {
+      mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, o2));
+      mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, o2));
+    }
+    const float mnA = fmaxf(mA, mxA), mnB = fmaxf(mB, mxB);
+    const bool noneA = mnA == -INFINITY, noneB = mnB == -INFINITY;
+    const float alA = noneA ? 1.f : va::fast_exp2(mA - mnA);
+    const float alB = noneB ? 1.f : va::fast_exp2(mB - mnB);
+    mA = mnA;
+    mB = mnB;
+    float sumA = 0.f, sumB = 0.f;
+#pragma unroll
+    for (int n = 0; n < kKeys / 8; ++n) {
+      s[n][0] = noneA ? 0.f : va::fast_exp2(s[n][0] - mnA);
+      s[n][1] = noneA ? 0.f : va::fast_exp2(s[n][1] - mnA);
+      s[n][2] = noneB ? 0.f : va::fast_exp2(s[n][2] - mnB);
+      s[n][3] = noneB ? 0.f : va::fast_exp2(s[n][3] - mnB);
+      sumA += s[n][0] + s[n][1];
+      sumB += s[n][2] + s[n][3];
+    }
+    lA = lA * alA + sumA;
+    lB = lB * alB + sumB;
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+      o[n][0] *= alA; o[n][1] *= alA;
+      o[n][2] *= alB; o[n][3] *= alB;
+    }
+    // ---- O += P V ----
+#pragma unroll
+    for (int kk = 0; kk < kKeys / 16; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_h2(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_h2(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_h2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_h2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int n = 0; n < D / 8; n += 2) {
+        const int key = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int col = n * 8 + (lane >> 4) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(b0, b1, b2, b3, vt + key * LD + col);
+        mma16816(o[n], pa, b0, b1);
+        mma16816(o[n + 1], pa, b2, b3);
+      }
+    }
+    __syncthreads();  // buffer `buf` is refilled by the next iteration's prefetch
+  }
+
+  // ---- normalise + store ----
+#pragma unroll
+  for (int o2 = 1; o2 < 4; o2 <<= 1) {
+    lA += __shfl_xor_sync(0xffffffffu, lA, o2);
+    lB += __shfl_xor_sync(0xffffffffu, lB, o2);
+  }
+  const int bad_from = s_bad_from;
+  if (bad_from != INT_MAX && tid == 0) va::raise_flag(a.err, VA_FLAG_BAD_BLOCK);
+  const float invA = lA > 0.f ? 1.f / lA : 0.f, invB = lB > 0.f ? 1.f / lB : 0.f;
+  const bool wA = posA >= 0 && posA < bad_from && tkA < nq;
+  const bool wB = posB >= 0 && posB < bad_from && tkB < nq;
+  const int gA = rA - tkA * GC, gB = rB - tkB * GC;
+  __half *oA = a.out + (int64_t)(t0 + tkA) * a.o_s_token + (int64_t)(head0 + gA) * a.o_s_head;
+  __half *oB = a.out + (int64_t)(t0 + tkB) * a.o_s_token + (int64_t)(head0 + gB) * a.o_s_head;
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) {
+    const int c = n * 8 + 2 * (lane & 3);
+    if (wA) *reinterpret_cast<uint32_t *>(oA + c) = pack_h2(o[n][0] * invA, o[n][1] * invA);
+    if (wB) *reinterpret_cast<uint32_t *>(oB + c) = pack_h2(o[n][2] * invB, o[n][3] * invB);
+  }
+}
+
+template <int D, int GC>
+int launch_t(const PrefillArgs &a, dim3 grid, cudaStream_t st) {
+  using S = PShape<D>;
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(paged_prefill_kernel<D, GC>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)S::kSmem) != cudaSuccess)
+      return VA_ERR_LAUNCH;
+    configured[dev] = 1;
+  }
+  paged_prefill_kernel<D, GC><<<grid, kThreads, S::kSmem, st>>>(a);
+  return va_host::launch_status();
+}
+
+template <int D>
+int launch_g(int gc, const PrefillArgs &a, dim3 grid, cudaStream_t st) {
+  switch (gc) {
+    case 1: return launch_t<D, 1>(a, grid, st);
+    case 2: return launch_t<D, 2>(a, grid, st);
+    case 3: return launch_t<D, 3>(a, grid, st);
+    case 4: return launch_t<D, 4>(a, grid, st);
+    case 5: return launch_t<D, 5>(a, grid, st);
+    case 6: return launch_t<D, 6>(a, grid, st);
+    case 7: return launch_t<D, 7>(a, grid, st);
+    case 8: return launch_t<D, 8>(a, grid, st);
+  }
+  return VA_ERR_UNSUPPORTED;
+}
+
+int group_chunk(int g) {
+  for (int c = 8; c >= 1; --c)
+    if (g % c == 0) return c;
+  return 1;
+}
+
+int64_t max_tiles_for(int64_t T, int64_t num_seqs, int TQ) {
+  int64_t m = (T + TQ - 1) / TQ + num_seqs;
+  return m < T ? m : T;
+}
+
+}  // namespace
+
+extern "C" size_t va_paged_prefill_workspace_size(int64_t num_tokens, int64_t num_seqs) {
+  if (num_tokens <= 0) return 0;
+  // worst case over group sizes: TQ >= 8 tokens
+  const int64_t mt = max_tiles_for(num_tokens, num_seqs, 8);
+  return 256 + (size_t)mt * sizeof(int2);
+}
+
+extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
+                                const void *v_cache, const int32_t *block_table,
+                                const int32_t *token_to_seq, const int32_t *positions,
+                                int64_t num_tokens, int64_t num_seqs, int num_query_heads,
+                                int num_kv_heads, int head_size, int block_size,
+                                int64_t max_blocks_per_seq, int64_t num_blocks, float scale,
+                                int64_t s_block, int64_t s_head, int64_t s_token,
+                                int64_t q_s_token, int64_t q_s_head, int64_t o_s_token,
+                                int64_t o_s_head, void *workspace, size_t workspace_bytes,
+                                int32_t *err_flag, void *stream) {
+  if (num_tokens < 0 || num_seqs < 0 || max_blocks_per_seq < 0 || num_blocks < 0)
+    return VA_ERR_INVALID_ARG;
+  if (num_tokens == 0) return VA_OK;
+  if (!out || !q || !k_cache || !v_cache || !block_table || !token_to_seq || !positions)
+    return VA_ERR_INVALID_ARG;
+  if (num_kv_heads <= 0 || num_query_heads <= 0 || num_query_heads % num_kv_heads)
+    return VA_ERR_INVALID_ARG;
+  if (head_size != 32 && head_size != 64 && head_size != 96 && head_size != 128)
+    return VA_ERR_UNSUPPORTED;
+  if (block_size <= 0 || block_size > kKeys || kKeys % block_size) return VA_ERR_UNSUPPORTED;
+  if (num_tokens > INT32_MAX / 2) return VA_ERR_UNSUPPORTED;
+  auto m8 = [](int64_t s) { return s % 8 == 0; };
+  if (!va_host::aligned16(q) || !va_host::aligned16(k_cache) || !va_host::aligned16(v_cache) ||
+      !va_host::aligned16(out) || !m8(s_block) || !m8(s_head) || !m8(s_token) ||
+      !m8(q_s_token) || !m8(q_s_head) || o_s_token % 2 || o_s_head % 2)
+    return VA_ERR_INVALID_ARG;
+  const size_t need = va_paged_prefill_workspace_size(num_tokens, num_seqs);
+  if (!workspace || workspace_bytes < need) return VA_ERR_WORKSPACE;
+
+  const int G = num_query_heads / num_kv_heads;
+  const int gc = group_chunk(G);
+  const int TQ = kRows / gc;
+  const int64_t mt = max_tiles_for(num_tokens, num_seqs, TQ);
+  if (mt > INT32_MAX) return VA_ERR_UNSUPPORTED;
+
+  unsigned char *ws = static_cast<unsigned char *>(workspace);
+  int32_t *tiles_n = reinterpret_cast<int32_t *>(ws);
+  int2 *tiles = reinterpret_cast<int2 *>(ws + 256);
+  auto st = static_cast<cudaStream_t>(stream);
+  plan_tiles_kernel<<<1, 1024, 0, st>>>(token_to_seq, num_tokens, TQ, tiles, tiles_n, mt,
+                                        err_flag);
+  if (va_host::launch_status() != VA_OK) return VA_ERR_LAUNCH;
+
+  PrefillArgs a{};
+  a.out = static_cast<__half *>(out);
+  a.q = static_cast<const __half *>(q);
+  a.kc = static_cast<const __half *>(k_cache);
+  a.vc = static_cast<const __half *>(v_cache);
+  a.bt = block_table;
+  a.tok_seq = token_to_seq;
+  a.pos = positions;
+  a.tiles = tiles;
+  a.tiles_n = tiles_n;
+  a.err = err_flag;
+  a.num_seqs = num_seqs;
+  a.max_blocks = max_blocks_per_seq;
+  a.num_blocks = num_blocks;
+  a.Hq = num_query_heads;
+  a.Hkv = num_kv_heads;
+  a.G = G;
+  a.hgroups = G / gc;
+  a.TQ = TQ;
+  a.bs = block_size;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.s_block = s_block; a.s_head = s_head; a.s_token = s_token;
+  a.q_s_token = q_s_token; a.q_s_head = q_s_head;
+  a.o_s_token = o_s_token; a.o_s_head = o_s_head;
+  const dim3 grid((unsigned)mt, (unsigned)(num_kv_heads * a.hgroups));
+  switch (head_size) {
+    case 32: return launch_g<32>(gc, a, grid, st);
+    case 64: return launch_g<64>(gc, a, grid, st);
+    case 96: return launch_g<96>(gc, a, grid, st);
+    case 128: return launch_g<128>(gc, a, grid, st);
+  }
+  return VA_ERR_UNSUPPORTED;
+}
