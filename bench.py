@@ -36,8 +36,9 @@ sys.path.insert(0, ROOT)
 
 import torch  # noqa: E402
 
-WORKLOAD = "devstral_b1024"
-METRIC = "paged-attn decode HBM GB/s (algorithmic bytes) at batch 1024, 22B shape"
+WORKLOAD = "devstral_b1024"  # default; --workload selects another decode config
+METRIC = "paged-attn decode HBM GB/s (algorithmic bytes)"
+GLOBAL_BATCH = 1024
 UNIT = "GB/s"
 
 
@@ -134,6 +135,8 @@ def dist_setup(n_gpus):
 def global_lengths():
     from vllm_apple_b200.workloads import DECODE_CONFIGS, draw_lengths
     c = DECODE_CONFIGS[WORKLOAD]
+    global GLOBAL_BATCH
+    GLOBAL_BATCH = c["batch"]
     gen = torch.Generator().manual_seed(0)
     return draw_lengths(c["dist"], c["batch"], gen)
 
@@ -192,6 +195,19 @@ def run_ours(args, world, rank, local):
     ops.check_device_errors(local)
 
     # ---- e2e through the engine op API with host buffers ----
+    if args.no_e2e:
+        e2e_ms_local, h2d, d2h = 0.0, 0, 0
+    else:
+        e2e_ms_local, h2d, d2h = run_e2e(args, case, local, dev, stream, barrier, q, nk, nv, bt,
+                                         sl, out, max_len)
+    return finish(args, world, rank, pg, case, ms_local, e2e_ms_local, h2d, d2h,
+                  launches_per_step, clk, dev)
+
+
+def run_e2e(args, case, local, dev, stream, barrier, q, nk, nv, bt, sl, out, max_len):
+    from vllm_apple_b200 import ops
+    from vllm_apple_b200.engine import EngineContext, PagedAttentionOp
+    B = case.batch
     ctx = EngineContext(local)
     op = PagedAttentionOp(ctx, case.Hkv, case.Hq, case.D, case.bs, case.scale)
     h_q, h_nk, h_nv = (t.pin_memory() for t in (case.q, case.new_k, case.new_v))
@@ -225,7 +241,11 @@ def run_ours(args, world, rank, local):
     barrier()
     e2e_ms_local = e0.elapsed_time(e1) / e2e_steps
     ops.check_device_errors(local)
+    return e2e_ms_local, h2d, d2h
 
+
+def finish(args, world, rank, pg, case, ms_local, e2e_ms_local, h2d, d2h, launches_per_step,
+           clk, dev):
     # ---- aggregate over ranks ----
     local_bytes = case.algorithmic_bytes()
     local_tokens = case.context_tokens
@@ -260,8 +280,9 @@ def run_ours(args, world, rank, local):
         "vs_baseline": None,
         "dtype": "f16",
         "data": "synthetic (seeded N(0,1) fp16 q/k/v, log-normal lengths)",
-        "config": {"workload": WORKLOAD + "_decode", "global_batch": 1024, "Hq": 32, "Hkv": 8,
-                   "head_size": 128, "block_size": 16, "ctx": "lognormal(2048,0.6) in [512,8192]",
+        "config": {"workload": WORKLOAD + "_decode", "global_batch": GLOBAL_BATCH,
+                   "Hq": case.Hq, "Hkv": case.Hkv, "head_size": case.D, "block_size": case.bs,
+                   "ctx": str(case.meta["dist"]),
                    "context_tokens": int(all_tokens), "sharding": "LPT by context length",
                    "layout": "engine [nb,Hkv,bs,D]",
                    "l2": "inputs larger than L2 (no flush)", "parallelism": f"seq-shard x{world}"},
@@ -270,14 +291,14 @@ def run_ours(args, world, rank, local):
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": traffic,
                      "algorithmic_bytes_per_launch": int(local_bytes)},
-        "e2e": {"value": round(all_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": UNIT,
-                "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": int(h2d),
-                "d2h_bytes_per_step": int(d2h),
-                "api": "engine PagedAttentionOp.encode_decode_fused"},
+        "e2e": None if args.no_e2e else {
+            "value": round(all_bytes / (e2e_ms * 1e-3) / 1e9, 1), "unit": UNIT,
+            "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h), "api": "engine PagedAttentionOp.encode_decode_fused"},
         "gpu_launches": args.steps * launches_per_step,
         "clocks": clk.summary(),
     }
-    if world == 1:
+    if world == 1 and args.cpu_budget > 0:
         res["cpu_baseline"] = cpu_baseline(budget_s=args.cpu_budget)
     if pg is not None:
         pg.destroy_process_group()
@@ -352,7 +373,7 @@ def run_reference(args, world, rank):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": WORKLOAD + "_decode", "global_batch": 1024,
+        "config": {"workload": WORKLOAD + "_decode", "global_batch": GLOBAL_BATCH,
                    "sample_seqs": n_seqs, "context_tokens": case.context_tokens},
         "seq_tokens_per_s": round(case.context_tokens / sec, 1),
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads,
@@ -365,13 +386,19 @@ def run_reference(args, world, rank):
 
 
 def main():
+    global WORKLOAD
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--cpu-budget", type=float, default=15.0,
+                    help="seconds of CPU-baseline timing (0 skips it)")
+    ap.add_argument("--workload", default=WORKLOAD,
+                    help="decode config of vllm_apple_b200.workloads (default: %(default)s)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
     args = ap.parse_args()
+    WORKLOAD = args.workload
     if args.warmup < 3:
         args.warmup = 3
     world, rank, local = dist_setup(args.gpus)

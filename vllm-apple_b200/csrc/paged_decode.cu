@@ -28,8 +28,16 @@
 
 namespace {
 
+// Tuning knobs (defaults are the measured best on B200; see profiles/).
+#ifndef VA_DECODE_STAGES
+#define VA_DECODE_STAGES 2
+#endif
+#ifndef VA_DECODE_DPL128
+#define VA_DECODE_DPL128 32
+#endif
+
 constexpr int kNW = 4;                     // warps per CTA
-constexpr int kStages = 3;                 // pages in flight per warp
+constexpr int kStages = VA_DECODE_STAGES;  // pages in flight per warp
 constexpr uint32_t kWaitLimit = 1u << 22;  // bounded mbarrier polls
 
 struct DecodeArgs {
@@ -51,7 +59,7 @@ constexpr int pow2ceil(int x) { return x <= 1 ? 1 : 2 * pow2ceil((x + 1) / 2); }
 
 template <int D>
 struct Shape {
-  static constexpr int DPL = (D == 96) ? 24 : 16;  // dims per lane in QK^T
+  static constexpr int DPL = (D == 96) ? 24 : (D == 128 ? VA_DECODE_DPL128 : 16);  // dims per lane in QK^T
   static constexpr int TPT = D / DPL;              // lanes sharing a token
   static constexpr int TOK = 32 / TPT;             // tokens per pass
   static constexpr int DV = (D == 96) ? 3 : D / 32;  // output dims per lane in PV
@@ -80,6 +88,20 @@ VA_DEVINL void load_v(const __half *row, int lane, float (&v)[Shape<D>::DV]) {
   } else {
     v[0] = __half2float(row[lane]);
   }
+}
+
+// Per-lane rotation of the order in which a lane walks its 16-byte chunks of a
+// K row (and, identically, of its q registers) so that the 8 lanes of each
+// shared-memory wavefront hit 8 distinct 16-byte bank groups.
+template <int D>
+VA_DEVINL int chunk_rot(int lane) {
+  constexpr int DPL = Shape<D>::DPL, TPT = Shape<D>::TPT;
+  const int cq = lane % TPT, tq = lane / TPT;
+  if constexpr (D == 96) return 0;                      // 12 chunks/row: already distinct
+  else if constexpr (DPL == 32) return ((cq >> 1) + 2 * (tq & 1)) & 3;  // D=128, 4 lanes/token
+  else if constexpr (TPT == 8) return (cq >> 2) & 1;    // D=128, 8 lanes/token
+  else if constexpr (TPT == 4) return tq & 1;           // D=64
+  else return (tq >> 1) & 1;                            // D=32
 }
 
 // Reduce-scatter N partial sums across the lanes that differ in bits
@@ -221,6 +243,8 @@ __global__ void __launch_bounds__(kNW * 32) paged_decode_kernel(const DecodeArgs
 
   // q of every head of the group, DPL dims of this lane's chunk, packed fp16.
   const int tq = lane / TPT, cq = lane % TPT;
+  constexpr int NCH = DPL / 8;  // 16-byte chunks per lane
+  const int rot = chunk_rot<D>(lane);
   uint32_t qr[GC][DPL / 2];
 #pragma unroll
   for (int h = 0; h < GC; ++h) {
@@ -228,8 +252,10 @@ __global__ void __launch_bounds__(kNW * 32) paged_decode_kernel(const DecodeArgs
                                                       (int64_t)(head0 + h) * a.q_s_head +
                                                       cq * DPL);
 #pragma unroll
-    for (int j = 0; j < DPL / 8; ++j) {
-      const uint4 v = __ldg(qp + j);
+    for (int j = 0; j < NCH; ++j) {
+      int c = j + rot;
+      if (c >= NCH) c -= NCH;
+      const uint4 v = __ldg(qp + c);
       qr[h][4 * j + 0] = v.x; qr[h][4 * j + 1] = v.y;
       qr[h][4 * j + 2] = v.z; qr[h][4 * j + 3] = v.w;
     }
@@ -292,28 +318,26 @@ __global__ void __launch_bounds__(kNW * 32) paged_decode_kernel(const DecodeArgs
         const int t = P * TOK + tq;
         const __half *krow = sk + t * D + cq * DPL;
         uint32_t kr[DPL / 2];
-        if constexpr (DPL == 16) {
-          // alternate which half is read first to keep 8-lane phases conflict-free
-          const int sw = (lane >> 2) & 1;
-          const uint4 x0 = *reinterpret_cast<const uint4 *>(krow + 8 * sw);
-          const uint4 x1 = *reinterpret_cast<const uint4 *>(krow + 8 * (sw ^ 1));
-          const uint4 lo = sw ? x1 : x0, hi = sw ? x0 : x1;
-          kr[0] = lo.x; kr[1] = lo.y; kr[2] = lo.z; kr[3] = lo.w;
-          kr[4] = hi.x; kr[5] = hi.y; kr[6] = hi.z; kr[7] = hi.w;
-        } else {
 #pragma unroll
-          for (int j = 0; j < DPL / 8; ++j) {
-            const uint4 x = *reinterpret_cast<const uint4 *>(krow + 8 * j);
-            kr[4 * j + 0] = x.x; kr[4 * j + 1] = x.y; kr[4 * j + 2] = x.z; kr[4 * j + 3] = x.w;
-          }
+        for (int j = 0; j < NCH; ++j) {
+          int c = j + rot;
+          if (c >= NCH) c -= NCH;
+          const uint4 x = *reinterpret_cast<const uint4 *>(krow + 8 * c);
+          kr[4 * j + 0] = x.x; kr[4 * j + 1] = x.y; kr[4 * j + 2] = x.z; kr[4 * j + 3] = x.w;
         }
-        float part[GP];
+        // two independent FMA chains per head, summed at the end
+        float part[GP], part2[GP];
 #pragma unroll
-        for (int h = 0; h < GP; ++h) part[h] = 0.f;
+        for (int h = 0; h < GP; ++h) { part[h] = 0.f; part2[h] = 0.f; }
 #pragma unroll
         for (int h = 0; h < GC; ++h)
 #pragma unroll
-          for (int j = 0; j < DPL / 2; ++j) va::fma2_f16_f32(part[h], qr[h][j], kr[j]);
+          for (int j = 0; j < DPL / 2; j += 2) {
+            va::fma2_f16_f32(part[h], qr[h][j], kr[j]);
+            va::fma2_f16_f32(part2[h], qr[h][j + 1], kr[j + 1]);
+          }
+#pragma unroll
+        for (int h = 0; h < GC; ++h) part[h] += part2[h];
         reduce_scatter<GP, TPT / 2>(part, lane);
         const bool valid = t < ntok;
 #pragma unroll
@@ -449,10 +473,11 @@ VA_DEVINL int64_t seq_splits(const DecodeArgs &a, int L_in, int bs, int grid_spl
   return nsplit > grid_splits ? grid_splits : nsplit;
 }
 
-// Merge the split partials of one (sequence, q-head group) in split order.
+// Merge the split partials of one (sequence, q-head group) in split order:
+// one thread per output element (block = group heads x head_size threads).
 template <int D>
-__global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeArgs a, int gc,
-                                                                   int bs) {
+__global__ void __launch_bounds__(1024) paged_decode_combine_kernel(const DecodeArgs a, int gc,
+                                                                    int bs) {
   const int seq = blockIdx.x;
   const int L_in = a.seq_lens[seq];
   if (L_in <= 0) return;
@@ -460,26 +485,24 @@ __global__ void __launch_bounds__(128) paged_decode_combine_kernel(const DecodeA
   if (nsplit <= 1) return;  // written directly by the main kernel
   const int kvh = blockIdx.y / a.hgroups;
   const int hg = blockIdx.y - kvh * a.hgroups;
-  const int head0 = kvh * a.G + hg * gc;
-  const int64_t part_base = ((int64_t)seq * a.Hq + head0) * a.max_splits;
-  for (int idx = threadIdx.x; idx < gc * D; idx += blockDim.x) {
-    const int h = idx / D, d = idx - (idx / D) * D;
-    const int64_t pb = part_base + (int64_t)h * a.max_splits;
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, a.ws_ml[2 * (pb + s)]);
-    float Ls = 0.f, A = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float ms = a.ws_ml[2 * (pb + s)];
-      if (ms != -INFINITY) {
-        const float e = va::fast_exp2(ms - M);
-        Ls = fmaf(a.ws_ml[2 * (pb + s) + 1], e, Ls);
-        A = fmaf(a.ws_acc[(pb + s) * D + d], e, A);
-      }
+  const int h = threadIdx.x / D, d = threadIdx.x - (threadIdx.x / D) * D;
+  if (h >= gc) return;
+  const int head = kvh * a.G + hg * gc + h;
+  const int64_t pb = ((int64_t)seq * a.Hq + head) * a.max_splits;
+  const float2 *ml = reinterpret_cast<const float2 *>(a.ws_ml) + pb;
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ml[s].x);
+  float Ls = 0.f, A = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const float2 v = ml[s];
+    if (v.x != -INFINITY) {
+      const float e = va::fast_exp2(v.x - M);
+      Ls = fmaf(v.y, e, Ls);
+      A = fmaf(a.ws_acc[(pb + s) * D + d], e, A);
     }
-    const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-    a.out[(int64_t)seq * a.o_s_token + (int64_t)(head0 + h) * a.o_s_head + d] =
-        __float2half_rn(A * inv);
   }
+  const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+  a.out[(int64_t)seq * a.o_s_token + (int64_t)head * a.o_s_head + d] = __float2half_rn(A * inv);
 }
 
 // ---------------------------------------------------------------------------
@@ -554,7 +577,7 @@ int launch_t(const DecodeArgs &a, dim3 grid, cudaStream_t st) {
   if (grid.x > 1) {
     const int st0 = va_host::launch_status();
     if (st0 != VA_OK) return st0;
-    paged_decode_combine_kernel<D><<<dim3(grid.z, grid.y), 128, 0, st>>>(a, GC, BS);
+    paged_decode_combine_kernel<D><<<dim3(grid.z, grid.y), GC * D, 0, st>>>(a, GC, BS);
   }
   return va_host::launch_status();
 }

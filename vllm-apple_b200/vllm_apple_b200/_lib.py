@@ -6,6 +6,7 @@ op raises -- there is no CPU or PyTorch fallback.
 from __future__ import annotations
 
 import ctypes
+import os
 from ctypes import c_float, c_int, c_int32, c_int64, c_size_t, c_void_p
 from pathlib import Path
 
@@ -71,11 +72,18 @@ class VAError(RuntimeError):
 
 
 def load(path: Path | str | None = None) -> ctypes.CDLL:
-    """Load (once) and declare the library; raises if it is not built."""
+    """Load (once) and declare the library; raises if it is not built.
+
+    ``VLLM_APPLE_B200_LIB`` may name an alternative build of the same ABI
+    (used for tuning sweeps); by default the in-tree build is loaded."""
     global _lib
-    if _lib is not None and path is None:
-        return _lib
-    p = Path(path) if path is not None else LIB_PATH
+    if path is None:
+        if _lib is not None:
+            return _lib
+        env = os.environ.get("VLLM_APPLE_B200_LIB")
+        p = Path(env) if env else LIB_PATH
+    else:
+        p = Path(path)
     if not p.exists():
         raise RuntimeError(
             f"{p} is missing: build the sm_100a library first "
