@@ -1,0 +1,90 @@
+"""The C-ABI library: loads without a GPU, exports every declared symbol, and
+its host-side planning entry points behave (no compute is launched here)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "vllm_apple_b200.h")
+
+
+def declared_symbols():
+    txt = open(HEADER).read()
+    return sorted(set(re.findall(r"VA_API\s+[\w\s\*]+?\b(va_\w+)\s*\(", txt)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from vllm_apple_b200 import _lib
+    return _lib.load()
+
+
+def test_header_declares_the_abi():
+    syms = declared_symbols()
+    for s in ("va_kv_write_slots", "va_kv_write_decode", "va_write_kv_batch", "va_paged_decode",
+              "va_paged_prefill", "va_rmsnorm", "va_rope", "va_silu_mul"):
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for s in declared_symbols():
+        assert hasattr(lib, s), f"{s} not exported"
+
+
+def test_ctypes_signatures_cover_the_header():
+    from vllm_apple_b200 import _lib
+    assert set(_lib.SIGNATURES) == set(declared_symbols())
+
+
+def test_version(lib):
+    assert b"sm_100a" in lib.va_version()
+
+
+def test_decode_workspace_size(lib):
+    f = lib.va_paged_decode_workspace_size
+    # a single short sequence never splits -> no workspace
+    assert f(1, 32, 8, 128, 16, 64) == 0
+    big = f(1024, 32, 8, 128, 16, 8192)
+    assert big > 0 and big % 256 == 0
+    assert f(0, 32, 8, 128, 16, 8192) == 0
+    assert f(4, 32, 5, 128, 16, 8192) == 0  # invalid head counts
+
+
+def test_prefill_workspace_size(lib):
+    assert lib.va_paged_prefill_workspace_size(0, 0) == 0
+    assert lib.va_paged_prefill_workspace_size(2108, 64) >= 256 + 8 * 2108 // 8
+
+
+def test_invalid_arguments_rejected_before_launch(lib):
+    # head counts that do not divide, null pointers, bad sizes: status 1, nothing launched
+    P = ctypes.c_void_p
+    assert lib.va_paged_decode(P(16), P(16), P(16), P(16), P(16), P(16), None, None, 4, 32, 5,
+                               128, 16, 8, 128, 64, 0.1, 0, 0, 0, 0, 0, 0, 0, 0, 0, None, 0,
+                               None, None) == 1
+    assert lib.va_kv_write_slots(None, None, None, None, None, 0, 5, 8, 128, 16, 4, 0, 0, 0, 0, 0,
+                                 None, None) == 1
+    assert lib.va_silu_mul(None, None, None, -1, None) == 1
+    assert lib.va_rope(None, None, None, None, None, 3, 2, 1, 64, 63, 10, 64, 64, 1, None,
+                       None) == 1
+    # zero-size work is a no-op success
+    assert lib.va_silu_mul(None, None, None, 0, None) == 0
+    assert lib.va_kv_write_slots(None, None, None, None, None, 0, 0, 8, 128, 16, 4, 0, 0, 0, 0, 0,
+                                 None, None) == 0
+
+
+def test_unsupported_shapes_reported(lib):
+    P = ctypes.c_void_p
+    # head_size 80 is not a compiled variant
+    assert lib.va_paged_decode(P(16), P(16), P(16), P(16), P(16), P(16), None, None, 4, 8, 8, 80,
+                               16, 8, 128, 64, 0.1, 0, 0, 0, 0, 0, 0, 0, 0, 0, None, 0, None,
+                               None) == 2
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    from vllm_apple_b200 import ops
+    x = torch.zeros(4, 8, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.silu_mul(x, x, x)

@@ -47,16 +47,9 @@ def draw_lengths(dist, n: int, gen: torch.Generator) -> torch.Tensor:
 
 
 def lpt_shard(lengths, world: int) -> list[list[int]]:
-    """Greedy longest-processing-time bin packing of sequences onto ``world``
-    ranks, balancing total context tokens (= KV bytes).  Deterministic."""
-    order = sorted(range(len(lengths)), key=lambda i: (-int(lengths[i]), i))
-    loads = [0] * world
-    bins: list[list[int]] = [[] for _ in range(world)]
-    for i in order:
-        r = min(range(world), key=lambda j: (loads[j], j))
-        bins[r].append(i)
-        loads[r] += int(lengths[i])
-    return [sorted(b) for b in bins]
+    """Sequences of each rank (greedy LPT on context length; see sharding.py)."""
+    from .sharding import lpt_partition
+    return lpt_partition(lengths, world)
 
 
 def assign_blocks(lengths, bs: int, pool_min: int, gen: torch.Generator):
