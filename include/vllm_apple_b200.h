@@ -12,6 +12,7 @@
  *   VA_ERR_UNSUPPORTED   2  shape outside the compiled variants (nothing launched)
  *   VA_ERR_LAUNCH        3  the CUDA launch itself failed
  *   VA_ERR_WORKSPACE     4  workspace missing or too small
+ *   VA_ERR_SCRATCH_LIMIT 5  shape needs more than the built-in scratch (nothing launched)
  *
  * Data-dependent problems found on the device (a slot or block id outside the
  * cache, a context longer than the block table, a bounded wait that ran out)
@@ -51,6 +52,7 @@ extern "C" {
 #define VA_ERR_UNSUPPORTED 2
 #define VA_ERR_LAUNCH 3
 #define VA_ERR_WORKSPACE 4
+#define VA_ERR_SCRATCH_LIMIT 5
 
 #define VA_FLAG_BAD_SLOT 0x1        /* slot >= num_blocks*block_size, or < -1 */
 #define VA_FLAG_BAD_BLOCK 0x2       /* block id < 0 or >= num_blocks inside a context */
@@ -143,6 +145,31 @@ VA_API int va_paged_decode(void *out, const void *q, void *k_cache, void *v_cach
                     int64_t o_s_head, int64_t new_s_token, int64_t new_s_head,
                     void *workspace, size_t workspace_bytes, int32_t *err_flag,
                     void *stream);
+
+/* va_paged_decode for callers that cannot allocate device memory: a host that
+ * only reaches this library through the C ABI and has no CUDA allocator of its
+ * own, or a serving loop whose memory is fixed up front and must not call
+ * cudaMalloc/cudaFree while running.  Same arguments and results as
+ * va_paged_decode minus the workspace: the split-KV partials go to a scratch
+ * array built into the library, VA_DECODE_STATIC_SCRATCH_BYTES per GPU, held by
+ * every GPU that loads the library until the process exits.  Shapes whose
+ * va_paged_decode_workspace_size exceeds it return VA_ERR_SCRATCH_LIMIT and
+ * launch nothing.  The first call on a device (with that device current)
+ * looks up the array's device address; make that first call before any stream
+ * capture.  All calls share the one array, so calls that overlap on the GPU
+ * (different streams, no ordering between them) race; calls ordered on one
+ * stream do not.  Allocates nothing.  It has no counterpart in the reference. */
+#define VA_DECODE_STATIC_SCRATCH_BYTES (32u << 20)
+VA_API int va_paged_decode_noalloc(void *out, const void *q, void *k_cache, void *v_cache,
+                                   const int32_t *block_table, const int32_t *seq_lens,
+                                   const void *new_k, const void *new_v, int64_t num_seqs,
+                                   int num_query_heads, int num_kv_heads, int head_size,
+                                   int block_size, int64_t max_blocks_per_seq,
+                                   int64_t max_seq_len, int64_t num_blocks, float scale,
+                                   int64_t s_block, int64_t s_head, int64_t s_token,
+                                   int64_t q_s_token, int64_t q_s_head, int64_t o_s_token,
+                                   int64_t o_s_head, int64_t new_s_token, int64_t new_s_head,
+                                   int32_t *err_flag, void *stream);
 
 /* Bytes of workspace va_paged_prefill needs (tile plan for num_tokens). */
 VA_API size_t va_paged_prefill_workspace_size(int64_t num_tokens, int64_t num_seqs);

@@ -24,6 +24,8 @@
 //     to the cache; no other CTA reads that slot.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
@@ -679,4 +681,62 @@ extern "C" int va_paged_decode(void *out, const void *q, void *k_cache, void *v_
     case 128: return launch_g<128, 16>(p.gc, a, grid, st);
   }
   return VA_ERR_UNSUPPORTED;
+}
+
+// ---------------------------------------------------------------------------
+// Decode without caller-provided scratch.
+//
+// For callers that cannot allocate device memory themselves -- a host that
+// reaches this library only through its C ABI (an FFI binding with no CUDA
+// allocator of its own), or a serving loop whose device memory is fixed up
+// front by another runtime and must not call cudaMalloc/cudaFree (which can
+// synchronise the device) once it is running.  The split-KV partials live in
+// the file-scope array below instead of a workspace argument.  Every GPU that
+// loads this library reserves VA_DECODE_STATIC_SCRATCH_BYTES for it until the
+// process exits.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_decode_scratch[VA_DECODE_STATIC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_scratch_mu;
+void *g_scratch_ptr[64] = {nullptr};
+}  // namespace
+
+extern "C" int va_paged_decode_noalloc(void *out, const void *q, void *k_cache, void *v_cache,
+                                       const int32_t *block_table, const int32_t *seq_lens,
+                                       const void *new_k, const void *new_v, int64_t num_seqs,
+                                       int num_query_heads, int num_kv_heads, int head_size,
+                                       int block_size, int64_t max_blocks_per_seq,
+                                       int64_t max_seq_len, int64_t num_blocks, float scale,
+                                       int64_t s_block, int64_t s_head, int64_t s_token,
+                                       int64_t q_s_token, int64_t q_s_head, int64_t o_s_token,
+                                       int64_t o_s_head, int64_t new_s_token,
+                                       int64_t new_s_head, int32_t *err_flag, void *stream) {
+  const size_t need = va_paged_decode_workspace_size(num_seqs, num_query_heads, num_kv_heads,
+                                                     head_size, block_size, max_seq_len);
+  if (need > (size_t)VA_DECODE_STATIC_SCRATCH_BYTES) return VA_ERR_SCRATCH_LIMIT;
+  void *ws = nullptr;
+  if (need) {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VA_ERR_LAUNCH;
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_ptr[dev]) {
+      // The array's host-side name is only a handle; its device address comes
+      // from the runtime, once per device, with that device current.
+      void *p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || !p) {
+        cudaGetLastError();
+        return VA_ERR_LAUNCH;
+      }
+      g_scratch_ptr[dev] = p;
+    }
+    ws = g_scratch_ptr[dev];
+  }
+  // The split partials need no initial value: the combine reads only what the
+  // main kernel of the same call wrote.
+  return va_paged_decode(out, q, k_cache, v_cache, block_table, seq_lens, new_k, new_v,
+                         num_seqs, num_query_heads, num_kv_heads, head_size, block_size,
+                         max_blocks_per_seq, max_seq_len, num_blocks, scale, s_block, s_head,
+                         s_token, q_s_token, q_s_head, o_s_token, o_s_head, new_s_token,
+                         new_s_head, ws, need, err_flag, stream);
 }

@@ -17,6 +17,7 @@ VA_ERR_INVALID_ARG = 1
 VA_ERR_UNSUPPORTED = 2
 VA_ERR_LAUNCH = 3
 VA_ERR_WORKSPACE = 4
+VA_ERR_SCRATCH_LIMIT = 5
 
 VA_FLAG_BAD_SLOT = 0x1
 VA_FLAG_BAD_BLOCK = 0x2
@@ -29,6 +30,7 @@ _STATUS = {
     VA_ERR_UNSUPPORTED: "shape outside the compiled sm_100a variants",
     VA_ERR_LAUNCH: "CUDA launch failed",
     VA_ERR_WORKSPACE: "workspace missing or too small",
+    VA_ERR_SCRATCH_LIMIT: "shape needs more than the library's built-in decode scratch",
 }
 
 FLAG_NAMES = {
@@ -54,6 +56,9 @@ SIGNATURES = {
     "va_paged_decode": (c_int, [P, P, P, P, P, P, P, P, I64, c_int, c_int, c_int, c_int, I64, I64,
                                 I64, c_float, I64, I64, I64, I64, I64, I64, I64, I64, I64, P,
                                 c_size_t, P, P]),
+    "va_paged_decode_noalloc": (c_int, [P, P, P, P, P, P, P, P, I64, c_int, c_int, c_int, c_int,
+                                        I64, I64, I64, c_float, I64, I64, I64, I64, I64, I64,
+                                        I64, I64, I64, P, P]),
     "va_paged_prefill_workspace_size": (c_size_t, [I64, I64]),
     "va_paged_prefill": (c_int, [P, P, P, P, P, P, P, I64, I64, c_int, c_int, c_int, c_int, I64,
                                  I64, c_float, I64, I64, I64, I64, I64, I64, I64, P, c_size_t, P,
