@@ -171,16 +171,22 @@ VA_API int va_paged_decode_noalloc(void *out, const void *q, void *k_cache, void
                                    int64_t o_s_head, int64_t new_s_token, int64_t new_s_head,
                                    int32_t *err_flag, void *stream);
 
-/* Bytes of workspace va_paged_prefill needs (tile plan for num_tokens). */
-VA_API size_t va_paged_prefill_workspace_size(int64_t num_tokens, int64_t num_seqs);
+/* Bytes of workspace va_paged_prefill needs: the tile plan and the split-KV
+ * partials of the one-token rows (decode rows of a mixed batch), which are
+ * routed to the decode kernel.  No initialisation needed. */
+VA_API size_t va_paged_prefill_workspace_size(int64_t num_tokens, int64_t num_seqs,
+                                              int num_query_heads, int num_kv_heads,
+                                              int head_size, int block_size,
+                                              int64_t max_blocks_per_seq);
 
 /* Token-parallel causal paged attention (prefill / chunked-prefill mixed batch).
  * Token t of sequence token_to_seq[t] attends to cache positions
  * 0..positions[t] (the new tokens' K/V already written, e.g. by
  * va_kv_write_slots).  Tokens with an invalid sequence, a negative position, a
  * context longer than the block table or a negative block inside the context
- * are skipped (out untouched).  Consecutive tokens of one sequence with
- * consecutive positions are processed as tensor-core tiles.
+ * are skipped (out untouched).  Runs of consecutive tokens of one sequence are
+ * processed as tensor-core tiles (tcgen05 UMMA for head_size 64/128); one-token
+ * runs go to the split-KV decode kernel.
  * Replaces PagedAttentionOp.encode_prefill
  * (vllm_apple/engine/ops/attention.py:290-367) -- kernel
  * paged_attention_v2_prefill (vllm_apple/metal/kernels/paged_attention_v2.metal:375-478). */

@@ -53,8 +53,9 @@ def test_decode_workspace_size(lib):
 
 
 def test_prefill_workspace_size(lib):
-    assert lib.va_paged_prefill_workspace_size(0, 0) == 0
-    assert lib.va_paged_prefill_workspace_size(2108, 64) >= 256 + 8 * 2108 // 8
+    assert lib.va_paged_prefill_workspace_size(0, 0, 32, 8, 128, 16, 512) == 0
+    # tile plan + one-token-row list + split partials of routed decode rows
+    assert lib.va_paged_prefill_workspace_size(2108, 64, 32, 8, 128, 16, 513) > 2108 * 8
 
 
 def test_invalid_arguments_rejected_before_launch(lib):

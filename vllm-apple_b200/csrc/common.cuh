@@ -115,6 +115,11 @@ VA_DEVINL float2 h2_to_f2(uint32_t v) {
   return __half22float2(h);
 }
 
+VA_DEVINL uint32_t pack_h2(float lo, float hi) {  // round-to-nearest fp16 pair
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
 VA_DEVINL float fast_exp2(float x) {  // hardware ex2.approx; exp2(-inf) = 0
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -55,7 +55,36 @@ struct DecodeArgs {
   float scale_log2;
   int64_t s_block, s_head, s_token, q_s_token, q_s_head, o_s_token, o_s_head, n_s_token,
       n_s_head;
+  // Row mode (one-token rows of a prefill batch): grid row r is token rows[r];
+  // its sequence is row_tok_seq[t] and its context positions 0..row_pos[t].
+  const int32_t *rows, *rows_n, *row_tok_seq, *row_pos;
+  int64_t row_num_seqs;
 };
+
+// Block-table row, context length and q/out row of grid row r; false = skip.
+VA_DEVINL bool decode_row(const DecodeArgs &a, int r, int bs, int &bt_seq, int &L_in,
+                          int64_t &qo) {
+  if (a.rows == nullptr) {
+    bt_seq = r;
+    L_in = a.seq_lens[r];
+    qo = r;
+    return L_in > 0;
+  }
+  if (r >= *a.rows_n) return false;
+  const int t = a.rows[r];
+  const int s = a.row_tok_seq[t];
+  const int p = a.row_pos[t];
+  if (s < 0 || s >= a.row_num_seqs || p < 0) return false;
+  if ((int64_t)((p + bs) / bs) > a.max_blocks) {  // prefill rule: such a token is skipped
+    if (threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0)
+      va::raise_flag(a.err, VA_FLAG_CTX_OVERFLOW);
+    return false;
+  }
+  bt_seq = s;
+  L_in = p + 1;
+  qo = t;
+  return true;
+}
 
 constexpr int pow2ceil(int x) { return x <= 1 ? 1 : 2 * pow2ceil((x + 1) / 2); }
 
@@ -165,9 +194,10 @@ __global__ void __launch_bounds__(kNW * 32) paged_decode_kernel(const DecodeArgs
   float *pbuf = reinterpret_cast<float *>(smem + C::kStageBytes + C::kBarBytes);
   float *abuf = pbuf + kNW * BS * GP;
 
-  const int seq = blockIdx.z;
-  const int L_in = a.seq_lens[seq];
-  if (L_in <= 0) return;
+  const int seq = blockIdx.z;  // index of the partials; = the sequence outside row mode
+  int bt_seq, L_in;
+  int64_t qo;
+  if (!decode_row(a, seq, BS, bt_seq, L_in, qo)) return;
   int64_t L = L_in;
   int64_t npages = (L + BS - 1) / BS;
   bool clamped = false;
@@ -204,7 +234,7 @@ __global__ void __launch_bounds__(kNW * 32) paged_decode_kernel(const DecodeArgs
 
   const int64_t span = pend - pbeg;
   const int nloc = span > warp ? (int)((span - warp + kNW - 1) / kNW) : 0;
-  const int32_t *bt_row = a.bt + (int64_t)seq * a.max_blocks;
+  const int32_t *bt_row = a.bt + (int64_t)bt_seq * a.max_blocks;
   const uint64_t policy = va::l2_policy_evict_first();
   const bool contiguous = (a.s_token == D);
 
@@ -250,7 +280,7 @@ __global__ void __launch_bounds__(kNW * 32) paged_decode_kernel(const DecodeArgs
   uint32_t qr[GC][DPL / 2];
 #pragma unroll
   for (int h = 0; h < GC; ++h) {
-    const uint4 *qp = reinterpret_cast<const uint4 *>(a.q + (int64_t)seq * a.q_s_token +
+    const uint4 *qp = reinterpret_cast<const uint4 *>(a.q + qo * a.q_s_token +
                                                       (int64_t)(head0 + h) * a.q_s_head +
                                                       cq * DPL);
 #pragma unroll
@@ -456,7 +486,7 @@ __global__ void __launch_bounds__(kNW * 32) paged_decode_kernel(const DecodeArgs
     }
     if (single) {
       const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-      a.out[(int64_t)seq * a.o_s_token + (int64_t)(head0 + h) * a.o_s_head + d] =
+      a.out[qo * a.o_s_token + (int64_t)(head0 + h) * a.o_s_head + d] =
           __float2half_rn(A * inv);
     } else {
       const int64_t pidx = part_base + (int64_t)h * a.max_splits + split;
@@ -481,8 +511,9 @@ template <int D>
 __global__ void __launch_bounds__(1024) paged_decode_combine_kernel(const DecodeArgs a, int gc,
                                                                     int bs) {
   const int seq = blockIdx.x;
-  const int L_in = a.seq_lens[seq];
-  if (L_in <= 0) return;
+  int bt_seq, L_in;
+  int64_t qo;
+  if (!decode_row(a, seq, bs, bt_seq, L_in, qo)) return;
   const int64_t nsplit = seq_splits(a, L_in, bs, a.max_splits);
   if (nsplit <= 1) return;  // written directly by the main kernel
   const int kvh = blockIdx.y / a.hgroups;
@@ -504,7 +535,7 @@ __global__ void __launch_bounds__(1024) paged_decode_combine_kernel(const Decode
     }
   }
   const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-  a.out[(int64_t)seq * a.o_s_token + (int64_t)head * a.o_s_head + d] = __float2half_rn(A * inv);
+  a.out[qo * a.o_s_token + (int64_t)head * a.o_s_head + d] = __float2half_rn(A * inv);
 }
 
 // ---------------------------------------------------------------------------
@@ -600,6 +631,66 @@ int launch_g(int gc, const DecodeArgs &a, dim3 grid, cudaStream_t st) {
 }
 
 }  // namespace
+
+namespace va_internal {
+
+// Workspace bytes of decode_rows for up to rows_bound rows.
+size_t decode_rows_workspace(int64_t rows_bound, int Hq, int Hkv, int D, int bs,
+                             int64_t max_blocks) {
+  if (rows_bound <= 0 || Hkv <= 0 || Hq % Hkv) return 0;
+  const Plan p = make_plan(rows_bound, Hq, Hkv, bs, max_blocks * bs);
+  return ws_layout(rows_bound, Hq, Hkv, D, p).total;
+}
+
+// Split-KV decode attention of one-token prefill rows (row mode).  The row list
+// and its length live on the device (written by the prefill planner).
+int decode_rows(void *out, const void *q, const void *kc, const void *vc, const int32_t *bt,
+                const int32_t *rows, const int32_t *rows_n, const int32_t *tok_seq,
+                const int32_t *pos, int64_t rows_bound, int64_t num_seqs, int Hq, int Hkv, int D,
+                int bs, int64_t max_blocks, int64_t num_blocks, float scale, int64_t s_block,
+                int64_t s_head, int64_t s_token, int64_t q_s_token, int64_t q_s_head,
+                int64_t o_s_token, int64_t o_s_head, void *ws, size_t ws_bytes, int32_t *err,
+                cudaStream_t st) {
+  if (rows_bound <= 0) return VA_OK;
+  if (rows_bound > 65535 || bs != 16) return VA_ERR_UNSUPPORTED;
+  const Plan p = make_plan(rows_bound, Hq, Hkv, bs, max_blocks * bs);
+  const WsLayout w = ws_layout(rows_bound, Hq, Hkv, D, p);
+  if (w.total && (!ws || ws_bytes < w.total)) return VA_ERR_WORKSPACE;
+  DecodeArgs a{};
+  a.out = static_cast<__half *>(out);
+  a.q = static_cast<const __half *>(q);
+  a.kc = const_cast<__half *>(static_cast<const __half *>(kc));
+  a.vc = const_cast<__half *>(static_cast<const __half *>(vc));
+  a.bt = bt;
+  unsigned char *wsb = static_cast<unsigned char *>(ws);
+  a.ws_acc = w.total ? reinterpret_cast<float *>(wsb + w.acc) : nullptr;
+  a.ws_ml = w.total ? reinterpret_cast<float *>(wsb + w.ml) : nullptr;
+  a.err = err;
+  a.max_blocks = max_blocks;
+  a.num_blocks = num_blocks;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.G = Hq / Hkv;
+  a.hgroups = p.hgroups;
+  a.pps = p.pps;
+  a.max_splits = p.max_splits;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.s_block = s_block; a.s_head = s_head; a.s_token = s_token;
+  a.q_s_token = q_s_token; a.q_s_head = q_s_head;
+  a.o_s_token = o_s_token; a.o_s_head = o_s_head;
+  a.rows = rows; a.rows_n = rows_n; a.row_tok_seq = tok_seq; a.row_pos = pos;
+  a.row_num_seqs = num_seqs;
+  const dim3 grid((unsigned)p.max_splits, (unsigned)(Hkv * p.hgroups), (unsigned)rows_bound);
+  switch (D) {
+    case 32: return launch_g<32, 16>(p.gc, a, grid, st);
+    case 64: return launch_g<64, 16>(p.gc, a, grid, st);
+    case 96: return launch_g<96, 16>(p.gc, a, grid, st);
+    case 128: return launch_g<128, 16>(p.gc, a, grid, st);
+  }
+  return VA_ERR_UNSUPPORTED;
+}
+
+}  // namespace va_internal
 
 extern "C" size_t va_paged_decode_workspace_size(int64_t num_seqs, int num_query_heads,
                                                  int num_kv_heads, int head_size,

@@ -20,6 +20,19 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "prefill_tc.cuh"
+
+namespace va_internal {  // split-KV decode of one-token rows (paged_decode.cu)
+size_t decode_rows_workspace(int64_t rows_bound, int Hq, int Hkv, int D, int bs,
+                             int64_t max_blocks);
+int decode_rows(void *out, const void *q, const void *kc, const void *vc, const int32_t *bt,
+                const int32_t *rows, const int32_t *rows_n, const int32_t *tok_seq,
+                const int32_t *pos, int64_t rows_bound, int64_t num_seqs, int Hq, int Hkv, int D,
+                int bs, int64_t max_blocks, int64_t num_blocks, float scale, int64_t s_block,
+                int64_t s_head, int64_t s_token, int64_t q_s_token, int64_t q_s_head,
+                int64_t o_s_token, int64_t o_s_head, void *ws, size_t ws_bytes, int32_t *err,
+                cudaStream_t st);
+}  // namespace va_internal
 
 namespace {
 
@@ -33,11 +46,12 @@ constexpr int kThreads = 128;
 __global__ void __launch_bounds__(1024) plan_tiles_kernel(const int32_t *token_to_seq,
                                                           int64_t T, int TQ, int2 *tiles,
                                                           int32_t *tiles_n, int64_t max_tiles,
+                                                          int32_t *singles, int32_t *singles_n,
                                                           int32_t *err) {
   __shared__ int warp_buf[32];
-  __shared__ int carry_max, carry_sum;
+  __shared__ int carry_max, carry_sum, n_single;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  if (tid == 0) { carry_max = 0; carry_sum = 0; }
+  if (tid == 0) { carry_max = 0; carry_sum = 0; n_single = 0; }
   __syncthreads();
   for (int64_t base = 0; base < T; base += 1024) {
     const int64_t t = base + tid;
@@ -98,9 +112,16 @@ __global__ void __launch_bounds__(1024) plan_tiles_kernel(const int32_t *token_t
   const int n = carry_sum < max_tiles ? carry_sum : (int)max_tiles;
   for (int i = tid; i < n; i += 1024) {
     const int next = (i + 1 < n) ? tiles[i + 1].x : (int)T;
-    tiles[i].y = next - tiles[i].x;
+    const int cnt = next - tiles[i].x;
+    tiles[i].y = cnt;
+    // one-token tiles (decode rows of a mixed batch) go to the split-KV decode kernel
+    if (singles && cnt == 1) singles[atomicAdd(&n_single, 1)] = tiles[i].x;
   }
-  if (tid == 0) *tiles_n = n;
+  __syncthreads();
+  if (tid == 0) {
+    *tiles_n = n;
+    if (singles_n) *singles_n = n_single;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -114,7 +135,7 @@ struct PrefillArgs {
   const int32_t *tiles_n;
   int32_t *err;
   int64_t num_seqs, max_blocks, num_blocks;
-  int Hq, Hkv, G, hgroups, TQ, bs;
+  int Hq, Hkv, G, hgroups, TQ, bs, skip_singles;
   float scale_log2;
   int64_t s_block, s_head, s_token, q_s_token, q_s_head, o_s_token, o_s_head;
 };
@@ -174,6 +195,7 @@ __global__ void __launch_bounds__(kThreads) paged_prefill_kernel(const PrefillAr
   if (tile >= *a.tiles_n) return;
   const int2 td = a.tiles[tile];
   const int t0 = td.x, nq = td.y;
+  if (nq == 1 && a.skip_singles) return;  // handled by the split-KV decode kernel
   const int seq = a.tok_seq[t0];
   const int kvh = blockIdx.y / a.hgroups, hg = blockIdx.y - (blockIdx.y / a.hgroups) * a.hgroups;
   const int head0 = kvh * a.G + hg * GC;
@@ -407,6 +429,38 @@ int launch_g(int gc, const PrefillArgs &a, dim3 grid, cudaStream_t st) {
   return VA_ERR_UNSUPPORTED;
 }
 
+template <int D, int GC>
+int launch_tc_t(const tc::Args &a, dim3 grid, cudaStream_t st) {
+  using S = tc::Smem<D>;
+  static int configured[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    if (cudaFuncSetAttribute(tc::paged_prefill_tc_kernel<D, GC>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)S::kBytes) != cudaSuccess)
+      return VA_ERR_LAUNCH;
+    configured[dev] = 1;
+  }
+  tc::paged_prefill_tc_kernel<D, GC><<<grid, tc::kThreads, S::kBytes, st>>>(a);
+  return va_host::launch_status();
+}
+
+template <int D>
+int launch_tc_g(int gc, const tc::Args &a, dim3 grid, cudaStream_t st) {
+  switch (gc) {
+    case 1: return launch_tc_t<D, 1>(a, grid, st);
+    case 2: return launch_tc_t<D, 2>(a, grid, st);
+    case 3: return launch_tc_t<D, 3>(a, grid, st);
+    case 4: return launch_tc_t<D, 4>(a, grid, st);
+    case 5: return launch_tc_t<D, 5>(a, grid, st);
+    case 6: return launch_tc_t<D, 6>(a, grid, st);
+    case 7: return launch_tc_t<D, 7>(a, grid, st);
+    case 8: return launch_tc_t<D, 8>(a, grid, st);
+  }
+  return VA_ERR_UNSUPPORTED;
+}
+
 int group_chunk(int g) {
   for (int c = 8; c >= 1; --c)
     if (g % c == 0) return c;
@@ -418,13 +472,52 @@ int64_t max_tiles_for(int64_t T, int64_t num_seqs, int TQ) {
   return m < T ? m : T;
 }
 
+bool use_tc_kernel(int head_size) {
+  static int force_legacy = -1;
+  if (force_legacy < 0) {
+    const char *e = getenv("VA_PREFILL_MMA_SYNC");
+    force_legacy = (e && atoi(e) != 0) ? 1 : 0;
+  }
+  return !force_legacy && (head_size == 64 || head_size == 128);
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Workspace layout of one prefill call: [counters | tiles | one-token rows | decode partials].
+struct PrefillPlan {
+  int TQ, gc;
+  bool tc, route;
+  int64_t mt;
+  size_t o_tiles, o_singles, o_dec, dec_bytes, total;
+};
+
+PrefillPlan prefill_plan(int64_t T, int64_t S, int Hq, int Hkv, int D, int bs, int64_t maxb) {
+  PrefillPlan p{};
+  p.gc = group_chunk(Hq / Hkv);
+  p.tc = use_tc_kernel(D);
+  p.TQ = (p.tc ? tc::kRows : kRows) / p.gc;
+  p.mt = max_tiles_for(T, S, p.TQ);
+  p.route = bs == 16 && p.mt <= 65535;
+  p.o_tiles = 256;
+  p.o_singles = p.o_tiles + align256((size_t)p.mt * sizeof(int2));
+  p.o_dec = p.o_singles + align256((size_t)p.mt * sizeof(int32_t));
+  p.dec_bytes = p.route ? va_internal::decode_rows_workspace(p.mt, Hq, Hkv, D, bs, maxb) : 0;
+  p.total = p.o_dec + p.dec_bytes;
+  return p;
+}
+
 }  // namespace
 
-extern "C" size_t va_paged_prefill_workspace_size(int64_t num_tokens, int64_t num_seqs) {
-  if (num_tokens <= 0) return 0;
-  // worst case over group sizes: TQ >= 8 tokens
-  const int64_t mt = max_tiles_for(num_tokens, num_seqs, 8);
-  return 256 + (size_t)mt * sizeof(int2);
+extern "C" size_t va_paged_prefill_workspace_size(int64_t num_tokens, int64_t num_seqs,
+                                                  int num_query_heads, int num_kv_heads,
+                                                  int head_size, int block_size,
+                                                  int64_t max_blocks_per_seq) {
+  if (num_tokens <= 0 || num_kv_heads <= 0 || num_query_heads <= 0 ||
+      num_query_heads % num_kv_heads)
+    return 0;
+  return prefill_plan(num_tokens, num_seqs, num_query_heads, num_kv_heads, head_size,
+                      block_size, max_blocks_per_seq)
+      .total;
 }
 
 extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
@@ -453,22 +546,34 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
       !va_host::aligned16(out) || !m8(s_block) || !m8(s_head) || !m8(s_token) ||
       !m8(q_s_token) || !m8(q_s_head) || o_s_token % 2 || o_s_head % 2)
     return VA_ERR_INVALID_ARG;
-  const size_t need = va_paged_prefill_workspace_size(num_tokens, num_seqs);
-  if (!workspace || workspace_bytes < need) return VA_ERR_WORKSPACE;
-
+  const PrefillPlan pl = prefill_plan(num_tokens, num_seqs, num_query_heads, num_kv_heads,
+                                      head_size, block_size, max_blocks_per_seq);
+  if (!workspace || workspace_bytes < pl.total) return VA_ERR_WORKSPACE;
   const int G = num_query_heads / num_kv_heads;
-  const int gc = group_chunk(G);
-  const int TQ = kRows / gc;
-  const int64_t mt = max_tiles_for(num_tokens, num_seqs, TQ);
+  const int gc = pl.gc;
+  const bool use_tc = pl.tc;
+  const int TQ = pl.TQ;
+  const int64_t mt = pl.mt;
   if (mt > INT32_MAX) return VA_ERR_UNSUPPORTED;
 
   unsigned char *ws = static_cast<unsigned char *>(workspace);
   int32_t *tiles_n = reinterpret_cast<int32_t *>(ws);
-  int2 *tiles = reinterpret_cast<int2 *>(ws + 256);
+  int32_t *singles_n = tiles_n + 1;
+  int2 *tiles = reinterpret_cast<int2 *>(ws + pl.o_tiles);
+  int32_t *singles = reinterpret_cast<int32_t *>(ws + pl.o_singles);
   auto st = static_cast<cudaStream_t>(stream);
   plan_tiles_kernel<<<1, 1024, 0, st>>>(token_to_seq, num_tokens, TQ, tiles, tiles_n, mt,
-                                        err_flag);
+                                        pl.route ? singles : nullptr,
+                                        pl.route ? singles_n : nullptr, err_flag);
   if (va_host::launch_status() != VA_OK) return VA_ERR_LAUNCH;
+  if (pl.route) {
+    const int rc = va_internal::decode_rows(
+        out, q, k_cache, v_cache, block_table, singles, singles_n, token_to_seq, positions, mt,
+        num_seqs, num_query_heads, num_kv_heads, head_size, block_size, max_blocks_per_seq,
+        num_blocks, scale, s_block, s_head, s_token, q_s_token, q_s_head, o_s_token, o_s_head,
+        ws + pl.o_dec, pl.dec_bytes, err_flag, st);
+    if (rc != VA_OK) return rc;
+  }
 
   PrefillArgs a{};
   a.out = static_cast<__half *>(out);
@@ -490,11 +595,24 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
   a.hgroups = G / gc;
   a.TQ = TQ;
   a.bs = block_size;
+  a.skip_singles = pl.route ? 1 : 0;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.s_block = s_block; a.s_head = s_head; a.s_token = s_token;
   a.q_s_token = q_s_token; a.q_s_head = q_s_head;
   a.o_s_token = o_s_token; a.o_s_head = o_s_head;
   const dim3 grid((unsigned)mt, (unsigned)(num_kv_heads * a.hgroups));
+  if (use_tc) {
+    tc::Args t{};
+    t.out = a.out; t.q = a.q; t.kc = a.kc; t.vc = a.vc; t.bt = a.bt; t.tok_seq = a.tok_seq;
+    t.pos = a.pos; t.tiles = a.tiles; t.tiles_n = a.tiles_n; t.err = a.err;
+    t.num_seqs = a.num_seqs; t.max_blocks = a.max_blocks; t.num_blocks = a.num_blocks;
+    t.Hq = a.Hq; t.Hkv = a.Hkv; t.G = a.G; t.hgroups = a.hgroups; t.TQ = a.TQ; t.bs = a.bs;
+    t.skip_singles = a.skip_singles;
+    t.scale_log2 = a.scale_log2; t.s_block = a.s_block; t.s_head = a.s_head;
+    t.s_token = a.s_token; t.q_s_token = a.q_s_token; t.q_s_head = a.q_s_head;
+    t.o_s_token = a.o_s_token; t.o_s_head = a.o_s_head;
+    return head_size == 64 ? launch_tc_g<64>(gc, t, grid, st) : launch_tc_g<128>(gc, t, grid, st);
+  }
   switch (head_size) {
     case 32: return launch_g<32>(gc, a, grid, st);
     case 64: return launch_g<64>(gc, a, grid, st);

@@ -59,7 +59,7 @@ SIGNATURES = {
     "va_paged_decode_noalloc": (c_int, [P, P, P, P, P, P, P, P, I64, c_int, c_int, c_int, c_int,
                                         I64, I64, I64, c_float, I64, I64, I64, I64, I64, I64,
                                         I64, I64, I64, P, P]),
-    "va_paged_prefill_workspace_size": (c_size_t, [I64, I64]),
+    "va_paged_prefill_workspace_size": (c_size_t, [I64, I64, c_int, c_int, c_int, c_int, I64]),
     "va_paged_prefill": (c_int, [P, P, P, P, P, P, P, I64, I64, c_int, c_int, c_int, c_int, I64,
                                  I64, c_float, I64, I64, I64, I64, I64, I64, I64, P, c_size_t, P,
                                  P]),

@@ -136,7 +136,9 @@ class PagedAttentionOp:
         out, _ = resolve(output_buffer, output_offset)
         kc, _ = resolve(key_buffer)
         vc, _ = resolve(value_buffer)
-        nbytes = lib.va_paged_prefill_workspace_size(num_tokens, num_seqs)
+        nbytes = lib.va_paged_prefill_workspace_size(num_tokens, num_seqs, self.num_query_heads,
+                                                     self.num_kv_heads, self.head_size,
+                                                     self.block_size, max_blocks_per_seq)
         ws = _ops.workspace(dev, "prefill", nbytes)
         _lib.check(lib.va_paged_prefill(
             out, q, kc, vc, resolve(block_table_buffer)[0], resolve(token_to_seq_buffer)[0],

@@ -236,7 +236,8 @@ def paged_prefill(out, q, k_cache, v_cache, block_table, token_to_seq, positions
     S = block_table.shape[0] if num_seqs is None else num_seqs
     mb = block_table.shape[1] if max_blocks_per_seq is None else max_blocks_per_seq
     lib = _lib.load()
-    nbytes = lib.va_paged_prefill_workspace_size(T, S)
+    nbytes = lib.va_paged_prefill_workspace_size(T, S, q.shape[1], g.num_kv_heads, q.shape[2],
+                                                 g.block_size, mb)
     ws = workspace(dev, "prefill", nbytes)
     _lib.check(lib.va_paged_prefill(
         out.data_ptr(), q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
