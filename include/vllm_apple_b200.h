@@ -201,6 +201,56 @@ VA_API int va_paged_prefill(void *out, const void *q, const void *k_cache, const
                      void *stream);
 
 /* ---------------------------------------------------------------------------
+ * Step-level ops around the attention call
+ * ------------------------------------------------------------------------- */
+
+/* Neox rotary embedding of q [T, Hq, D] and k [T, Hkv, D] (in place, rot = D)
+ * fused with the scatter of the rotated k and of v [T, Hkv, D] into the paged
+ * cache by slot (-1 = padding, skipped): one pass over k and v instead of a
+ * RoPE pass and a KV-write pass.  Tokens with a position outside
+ * [0, max_position) are left untouched (VA_FLAG_BAD_POSITION).
+ * Replaces the sequence EngineRoPE.encode + KVWriteOp.encode_prefill of the
+ * reference runner (vllm_apple/engine/runner.py:942-1055; kernels
+ * rope_neox_kernel, vllm_apple/engine/ops/elementwise.py:185-239, and
+ * kv_write_prefill, vllm_apple/engine/ops/kv_write.py:118-156). */
+VA_API int va_rope_kv_write_slots(void *q, void *k, const void *v, void *k_cache, void *v_cache,
+                                  const float *cos_cache, const float *sin_cache,
+                                  const int32_t *positions, const void *slot_mapping,
+                                  int slot_is_i64, int64_t num_tokens, int num_heads,
+                                  int num_kv_heads, int head_size, int block_size,
+                                  int64_t num_blocks, int64_t max_position, int64_t q_s_token,
+                                  int64_t k_s_token, int64_t v_s_token, int64_t s_block,
+                                  int64_t s_head, int64_t s_token, int32_t *err_flag,
+                                  void *stream);
+
+/* Per-token prefill metadata on the device: for tokens first_token ..
+ * first_token+num_tokens-1 of a batch laid out by query_start_loc
+ * (int32 [num_seqs+1]), token_to_seq[t] = its sequence and positions[t] =
+ * seq_lens[s] - query_len(s) + (index within the sequence's new tokens);
+ * slot_mapping (optional, int64) = block_table[s][pos/bs]*bs + pos%bs or -1.
+ * Replaces the host-side derivation in the reference runner
+ * (vllm_apple/engine/runner.py:526-546, :642-683). */
+VA_API int va_build_prefill_metadata(const int32_t *query_start_loc, const int32_t *seq_lens,
+                                     const int32_t *block_table, int64_t num_seqs,
+                                     int64_t first_token, int64_t num_tokens,
+                                     int64_t max_blocks_per_seq, int block_size,
+                                     int32_t *token_to_seq, int32_t *positions,
+                                     int64_t *slot_mapping, void *stream);
+
+/* Copy every active block -- block_table[s][i] for i < ceil(seq_lens[s]/bs),
+ * ids in [0, num_blocks) -- of K and V from one cache layout to another
+ * (strides in elements, e.g. vLLM (nb, bs, H, D) -> engine [nb, H, bs, D]).
+ * Bit-exact.  Replaces EngineKVCache.sync_from_torch_cache
+ * (vllm_apple/engine/kv_cache.py:518-684). */
+VA_API int va_kv_sync_blocks(const void *src_k, const void *src_v, void *dst_k, void *dst_v,
+                             const int32_t *block_table, const int32_t *seq_lens,
+                             int64_t num_seqs, int64_t max_blocks_per_seq, int num_kv_heads,
+                             int head_size, int block_size, int64_t num_blocks,
+                             int64_t src_s_block, int64_t src_s_head, int64_t src_s_token,
+                             int64_t dst_s_block, int64_t dst_s_head, int64_t dst_s_token,
+                             void *stream);
+
+/* ---------------------------------------------------------------------------
  * Elementwise ops around the attention step
  * ------------------------------------------------------------------------- */
 

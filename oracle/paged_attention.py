@@ -323,3 +323,60 @@ def silu_mul(gate, up):
     g = np.asarray(gate).astype(np.float64)
     u = np.asarray(up).astype(np.float64)
     return g / (1.0 + np.exp(-g)) * u
+
+
+# --------------------------------------------------------------------------
+# step-level helpers
+# --------------------------------------------------------------------------
+
+
+def prefill_metadata(query_start_loc, seq_lens, block_table, block_size):
+    """(token_to_seq, positions, slot_mapping) of a batch laid out by query_start_loc.
+
+    token_to_seq follows the reference runner (vllm_apple/engine/runner.py:526-546,
+    :642-683: repeat_interleave of sequence ids by query length); the i-th new
+    token of sequence s sits at position seq_lens[s] - query_len + i and its slot
+    is block_table[s][pos // bs] * bs + pos % bs (-1 when the block is unused).
+    """
+    qsl = np.asarray(query_start_loc).astype(np.int64)
+    L = np.asarray(seq_lens).astype(np.int64)
+    bt = np.asarray(block_table).astype(np.int64)
+    lens = qsl[1:] - qsl[:-1]
+    if np.any(lens < 0):
+        raise ValueError("query_start_locs must be non-decreasing")
+    tok = np.repeat(np.arange(len(lens)), lens)
+    pos = np.concatenate([np.arange(L[s] - n, L[s]) for s, n in enumerate(lens)]) \
+        if len(tok) else np.zeros(0, np.int64)
+    slots = np.full(len(tok), -1, np.int64)
+    for t, (s, p) in enumerate(zip(tok, pos)):
+        if p >= 0 and p // block_size < bt.shape[1] and bt[s, p // block_size] >= 0:
+            slots[t] = bt[s, p // block_size] * block_size + p % block_size
+    return tok.astype(np.int32), pos.astype(np.int32), slots
+
+
+def kv_sync_blocks(src_k, src_v, dst_k, dst_v, block_table, seq_lens, src_layout="nhd",
+                   dst_layout="hnd"):
+    """Copy every active block from one cache layout to the other, in place.
+
+    Follows EngineKVCache.sync_from_torch_cache (vllm_apple/engine/kv_cache.py:
+    518-684): the active blocks are block_table[s][i] for i < ceil(seq_len/bs)
+    (capped at the table width), ids >= 0; ids beyond the cache are skipped; each
+    copied block is the (bs, H, D) -> (H, bs, D) permutation of the source.
+    """
+    nb, H, bs, D = cache_geometry(src_k, src_layout)
+    bt = np.asarray(block_table)
+    active = set()
+    for s, L in enumerate(np.asarray(seq_lens).reshape(-1)):
+        n = (int(L) + bs - 1) // bs
+        for i in range(min(n, bt.shape[1])):
+            b = int(bt[s, i])
+            if b >= 0:
+                active.add(b)
+    for b in active:
+        if b >= nb:
+            continue
+        for hh in range(H):
+            for t in range(bs):
+                _row(dst_k, dst_layout, b, hh, t)[...] = _row(src_k, src_layout, b, hh, t)
+                _row(dst_v, dst_layout, b, hh, t)[...] = _row(src_v, src_layout, b, hh, t)
+    return dst_k, dst_v

@@ -42,13 +42,15 @@ def test_impl_error_behaviour():
         impl.forward(None, out, out, out, None, None, out, output_scale=torch.ones(1))
 
 
+@pytest.mark.gpu
 def test_prefill_rows_chunked_positions():
     a = _mod()
     md = a.MetalAttentionMetadata(
         num_actual_tokens=5, max_query_len=3, query_start_loc=torch.tensor([0, 1, 2, 5]),
-        max_seq_len=40, seq_lens=torch.tensor([10, 20, 40]), block_table=None,
-        slot_mapping=None, scheduler_metadata=None, num_decode_tokens=2)
-    tok, pos = md.prefill_rows("cpu")
+        max_seq_len=40, seq_lens=torch.tensor([10, 20, 40]),
+        block_table=torch.zeros(3, 3, dtype=torch.int32), slot_mapping=None,
+        scheduler_metadata=None, num_decode_tokens=2)
+    tok, pos = md.prefill_rows("cuda")
     assert tok.tolist() == [2, 2, 2] and pos.tolist() == [37, 38, 39]
 
 

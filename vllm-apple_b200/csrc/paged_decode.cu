@@ -523,15 +523,42 @@ __global__ void __launch_bounds__(1024) paged_decode_combine_kernel(const Decode
   const int head = kvh * a.G + hg * gc + h;
   const int64_t pb = ((int64_t)seq * a.Hq + head) * a.max_splits;
   const float2 *ml = reinterpret_cast<const float2 *>(a.ws_ml) + pb;
+  const float *acc = a.ws_acc + pb * D + d;
+  // all loads of up to kU splits issued before any use: one memory latency
+  constexpr int kU = 16;
+  float mv[kU], lv[kU], av[kU];
+#pragma unroll
+  for (int s = 0; s < kU; ++s) {
+    if (s < nsplit) {
+      const float2 v = __ldcs(ml + s);
+      mv[s] = v.x;
+      lv[s] = v.y;
+      av[s] = __ldcs(acc + (int64_t)s * D);
+    } else {
+      mv[s] = -INFINITY;
+      lv[s] = 0.f;
+      av[s] = 0.f;
+    }
+  }
   float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ml[s].x);
+#pragma unroll
+  for (int s = 0; s < kU; ++s) M = fmaxf(M, mv[s]);
+  for (int s = kU; s < nsplit; ++s) M = fmaxf(M, ml[s].x);
   float Ls = 0.f, A = 0.f;
-  for (int s = 0; s < nsplit; ++s) {
+#pragma unroll
+  for (int s = 0; s < kU; ++s) {
+    if (mv[s] != -INFINITY) {
+      const float e = va::fast_exp2(mv[s] - M);
+      Ls = fmaf(lv[s], e, Ls);
+      A = fmaf(av[s], e, A);
+    }
+  }
+  for (int s = kU; s < nsplit; ++s) {
     const float2 v = ml[s];
     if (v.x != -INFINITY) {
       const float e = va::fast_exp2(v.x - M);
       Ls = fmaf(v.y, e, Ls);
-      A = fmaf(a.ws_acc[(pb + s) * D + d], e, A);
+      A = fmaf(acc[(int64_t)s * D], e, A);
     }
   }
   const float inv = Ls > 0.f ? 1.f / Ls : 0.f;

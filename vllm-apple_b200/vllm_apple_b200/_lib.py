@@ -63,6 +63,11 @@ SIGNATURES = {
     "va_paged_prefill": (c_int, [P, P, P, P, P, P, P, I64, I64, c_int, c_int, c_int, c_int, I64,
                                  I64, c_float, I64, I64, I64, I64, I64, I64, I64, P, c_size_t, P,
                                  P]),
+    "va_rope_kv_write_slots": (c_int, [P, P, P, P, P, P, P, P, P, c_int, I64, c_int, c_int, c_int,
+                                       c_int, I64, I64, I64, I64, I64, I64, I64, I64, P, P]),
+    "va_build_prefill_metadata": (c_int, [P, P, P, I64, I64, I64, I64, c_int, P, P, P, P]),
+    "va_kv_sync_blocks": (c_int, [P, P, P, P, P, P, I64, I64, c_int, c_int, c_int, I64, I64, I64,
+                                  I64, I64, I64, I64, P]),
     "va_rmsnorm": (c_int, [P, P, P, P, I64, I64, c_float, I64, I64, I64, P]),
     "va_rope": (c_int, [P, P, P, P, P, I64, c_int, c_int, c_int, c_int, I64, I64, I64, c_int, P,
                         P]),

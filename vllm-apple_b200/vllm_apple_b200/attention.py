@@ -154,21 +154,17 @@ class MetalAttentionMetadata:
     def prefill_rows(self, device):
         """(token_to_seq, positions) int32 on ``device`` for tokens
         num_decode_tokens..num_actual_tokens-1 (sequence index is absolute); the
-        i-th new token of a sequence sits at position seq_len - query_len + i."""
+        i-th new token of a sequence sits at position seq_len - query_len + i.
+        Built once per step on the device and shared by every layer."""
         if self._prefill_token_to_seq is None:
-            qsl, sl = self.query_start_loc_cpu, self.seq_lens_cpu
+            qsl = self.query_start_loc.to(device=device, dtype=torch.int32)
+            sl = self.seq_lens.to(device=device, dtype=torch.int32)
+            bt = self.block_table.to(device=device, dtype=torch.int32).contiguous()
             nd = self.num_decode_tokens
-            tok, pos = [], []
-            for s in range(len(qsl) - 1):
-                a, b = qsl[s], qsl[s + 1]
-                if b <= nd or b == a:
-                    continue
-                n_full = b - a
-                for i in range(max(a, nd) - a, n_full):
-                    tok.append(s)
-                    pos.append(sl[s] - n_full + i)
-            self._prefill_token_to_seq = torch.tensor(tok, dtype=torch.int32, device=device)
-            self._prefill_positions = torch.tensor(pos, dtype=torch.int32, device=device)
+            tok, pos, _ = ops.build_prefill_metadata(qsl.contiguous(), sl.contiguous(), bt,
+                                                     self.num_actual_tokens - nd,
+                                                     first_token=nd, with_slots=False)
+            self._prefill_token_to_seq, self._prefill_positions = tok, pos
         return self._prefill_token_to_seq, self._prefill_positions
 
 

@@ -96,6 +96,21 @@ class EngineKVCache:
         if bad.any():
             raise ValueError(f"Slot mapping contains invalid index {sm[bad].min()}{sfx}")
 
+    def sync_from_torch_cache(self, torch_caches, block_table, seq_lens) -> None:
+        """Copy the active blocks of vLLM-layout caches ``[2, nb, bs, H, D]`` (one per
+        layer) into the engine caches, on the device (reference kv_cache.py:518-684;
+        there the copy is a host loop over blocks)."""
+        from .. import ops
+        if len(torch_caches) != self._desc.num_layers:
+            raise ValueError(f"torch_caches has {len(torch_caches)} layers, "
+                             f"expected {self._desc.num_layers}")
+        dev = self._k[0].device
+        bt = block_table.to(device=dev, dtype=torch.int32).contiguous()
+        sl = seq_lens.to(device=dev, dtype=torch.int32).contiguous()
+        for layer, kv in enumerate(torch_caches):
+            ops.kv_sync_blocks(kv[0], kv[1], self._k[layer], self._v[layer], bt, sl,
+                               src_layout="nhd", dst_layout="hnd")
+
     def get_slot_offset(self, slot_idx: int):
         return divmod(int(slot_idx), self._desc.block_size)
 

@@ -221,6 +221,29 @@ class KVWriteOp:
             _err(step_ctx), step_ctx.stream_handle), "va_kv_write_slots")
         step_ctx.note_dispatch()
 
+    def encode_prefill_with_rope(self, step_ctx, rope: "EngineRoPE", query_buffer,
+                                 new_keys_buffer, new_values_buffer, key_buffer, value_buffer,
+                                 slot_mapping_buffer, positions_buffer, num_tokens: int,
+                                 query_offset: int = 0, new_keys_offset: int = 0,
+                                 new_values_offset: int = 0) -> None:
+        """RoPE of Q and K (in place) fused with the K/V scatter by slot: the
+        reference encodes EngineRoPE.encode then encode_prefill (runner.py:942-1055)."""
+        step_ctx.require_encoding("encode_prefill_with_rope()")
+        if not rope.is_neox_style or rope.rotary_dim != self.head_size:
+            raise ValueError("the fused path covers Neox RoPE over the whole head")
+        is64 = int(buffer_dtype(slot_mapping_buffer) == torch.int64)
+        D = self.head_size
+        _lib.check(_lib.load().va_rope_kv_write_slots(
+            resolve(query_buffer, query_offset)[0], resolve(new_keys_buffer, new_keys_offset)[0],
+            resolve(new_values_buffer, new_values_offset)[0], resolve(key_buffer)[0],
+            resolve(value_buffer)[0], rope._cos_cache.data_ptr(), rope._sin_cache.data_ptr(),
+            resolve(positions_buffer)[0], resolve(slot_mapping_buffer)[0], is64, num_tokens,
+            rope.num_heads, self.num_kv_heads, D, self.block_size, self._num_blocks(key_buffer),
+            rope.max_position, rope.num_heads * D, self.num_kv_heads * D, self.num_kv_heads * D,
+            self.kv_stride_block, self.kv_stride_head, self.kv_stride_token, _err(step_ctx),
+            step_ctx.stream_handle), "va_rope_kv_write_slots")
+        step_ctx.note_dispatch()
+
     def get_params_dict(self) -> Dict[str, Any]:
         return {"num_kv_heads": self.num_kv_heads, "head_size": self.head_size,
                 "block_size": self.block_size, "decode_kernel": "va_kv_write_decode",

@@ -299,3 +299,64 @@ def silu_mul(out, gate, up, num_elements=None):
     n = gate.numel() if num_elements is None else num_elements
     _lib.check(_lib.load().va_silu_mul(out.data_ptr(), gate.data_ptr(), up.data_ptr(), n,
                                        _stream(dev)), "va_silu_mul")
+
+
+# ---------------------------------------------------------------------------
+# step-level ops
+# ---------------------------------------------------------------------------
+def rope_kv_write_slots(q, k, v, k_cache, v_cache, cos_cache, sin_cache, positions,
+                        slot_mapping, layout="hnd"):
+    """Neox RoPE of q/k in place + scatter of rotated k and v into the cache by slot."""
+    dev = _dev_index(q)
+    g = cache_geom(k_cache, layout)
+    q_st, _ = _rows3(q, "q")
+    k_st, _ = _rows3(k, "k")
+    v_st, _ = _rows3(v, "v")
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        if t.stride(1) != t.shape[2]:
+            raise ValueError(f"{n} heads must be packed (head stride == head_size)")
+    _i32(positions, "positions")
+    if slot_mapping.dtype not in (torch.int32, torch.int64) or not slot_mapping.is_contiguous():
+        raise TypeError("slot_mapping must be a contiguous int32 or int64 tensor")
+    _lib.check(_lib.load().va_rope_kv_write_slots(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+        cos_cache.data_ptr(), sin_cache.data_ptr(), positions.data_ptr(), slot_mapping.data_ptr(),
+        int(slot_mapping.dtype == torch.int64), q.shape[0], q.shape[1], k.shape[1], q.shape[2],
+        g.block_size, g.num_blocks, cos_cache.shape[0], q_st, k_st, v_st, g.s_block, g.s_head,
+        g.s_token, err_flag(dev).data_ptr(), _stream(dev)), "va_rope_kv_write_slots")
+
+
+def build_prefill_metadata(query_start_loc, seq_lens, block_table, num_tokens, first_token=0,
+                           block_size=16, with_slots=True):
+    """(token_to_seq int32, positions int32, slot_mapping int64 | None) on the device."""
+    dev = _dev_index(seq_lens)
+    _i32(query_start_loc, "query_start_loc")
+    _i32(seq_lens, "seq_lens")
+    _i32(block_table, "block_table")
+    d = seq_lens.device
+    ts = torch.empty(num_tokens, dtype=torch.int32, device=d)
+    ps = torch.empty(num_tokens, dtype=torch.int32, device=d)
+    sm = torch.empty(num_tokens, dtype=torch.int64, device=d) if with_slots else None
+    _lib.check(_lib.load().va_build_prefill_metadata(
+        query_start_loc.data_ptr(), seq_lens.data_ptr(), block_table.data_ptr(),
+        seq_lens.numel(), first_token, num_tokens, block_table.shape[1], block_size,
+        ts.data_ptr(), ps.data_ptr(), _ptr(sm), _stream(dev)), "va_build_prefill_metadata")
+    return ts, ps, sm
+
+
+def kv_sync_blocks(src_k, src_v, dst_k, dst_v, block_table, seq_lens, src_layout="nhd",
+                   dst_layout="hnd"):
+    """Copy the active blocks of every sequence between cache layouts (bit-exact)."""
+    dev = _dev_index(src_k)
+    s = cache_geom(src_k, src_layout)
+    d = cache_geom(dst_k, dst_layout)
+    if (s.num_blocks, s.num_kv_heads, s.block_size, s.head_size) != (
+            d.num_blocks, d.num_kv_heads, d.block_size, d.head_size):
+        raise ValueError("source and destination caches differ in geometry")
+    _i32(block_table, "block_table")
+    _i32(seq_lens, "seq_lens")
+    _lib.check(_lib.load().va_kv_sync_blocks(
+        src_k.data_ptr(), src_v.data_ptr(), dst_k.data_ptr(), dst_v.data_ptr(),
+        block_table.data_ptr(), seq_lens.data_ptr(), seq_lens.numel(), block_table.shape[1],
+        s.num_kv_heads, s.head_size, s.block_size, s.num_blocks, s.s_block, s.s_head, s.s_token,
+        d.s_block, d.s_head, d.s_token, _stream(dev)), "va_kv_sync_blocks")
