@@ -58,12 +58,12 @@ def test_noalloc_decode_matches_workspace_decode(config, batch):
 def test_noalloc_rejects_shapes_beyond_its_scratch():
     from vllm_apple_b200 import _lib
     lib = _lib.load()
-    # 4096 sequences of up to 8192 tokens need far more split scratch than is built in
-    need = lib.va_paged_decode_workspace_size(4096, 32, 8, 128, 16, 8192)
+    # 4096 sequences of up to 65536 tokens need far more split scratch than is built in
+    need = lib.va_paged_decode_workspace_size(4096, 32, 8, 128, 16, 65536)
     assert need > (32 << 20)
     P = ctypes.c_void_p
     rc = lib.va_paged_decode_noalloc(P(256), P(256), P(256), P(256), P(256), P(256), None, None,
-                                     4096, 32, 8, 128, 16, 512, 8192, 1 << 20, 0.1,
+                                     4096, 32, 8, 128, 16, 4096, 65536, 1 << 20, 0.1,
                                      8 * 16 * 128, 16 * 128, 128, 4096, 128, 4096, 128, 0, 0,
                                      None, None)
     assert rc == _lib.VA_ERR_SCRATCH_LIMIT

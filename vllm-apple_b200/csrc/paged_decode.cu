@@ -578,7 +578,8 @@ int largest_group_divisor(int g) {
   return 1;
 }
 
-Plan make_plan(int64_t num_seqs, int Hq, int Hkv, int block_size, int64_t max_seq_len) {
+Plan make_plan(int64_t num_seqs, int Hq, int Hkv, int head_size, int block_size,
+               int64_t max_seq_len) {
   Plan p{};
   const int G = Hq / Hkv;
   p.gc = largest_group_divisor(G);
@@ -592,11 +593,14 @@ Plan make_plan(int64_t num_seqs, int Hq, int Hkv, int block_size, int64_t max_se
   }
   int pps = env_pps;
   if (pps <= 0) {
-    const int64_t target = 16LL * va_host::sm_count();
-    const int choices[] = {64, 32, 16, 8, 4};
+    // Largest split (fewest partials, fewest idle CTAs) whose worst-case CTA count
+    // still reaches a head-size-dependent floor; measured on B200 (batch 128 ->
+    // 64 pages, batch 1024 -> 512, Qwen-shape batch 64 -> 16).
+    const int64_t floor_units = head_size >= 128 ? 8192 : (head_size >= 96 ? 4096 : 2048);
+    const int choices[] = {512, 256, 128, 64, 32, 16, 8, 4};
     pps = 4;
     for (int c : choices)
-      if (base * ((npmax + c - 1) / c) >= target) { pps = c; break; }
+      if (base * ((npmax + c - 1) / c) >= floor_units) { pps = c; break; }
   }
   p.pps = pps;
   const int64_t ms = npmax > 0 ? (npmax + pps - 1) / pps : 1;
@@ -665,7 +669,7 @@ namespace va_internal {
 size_t decode_rows_workspace(int64_t rows_bound, int Hq, int Hkv, int D, int bs,
                              int64_t max_blocks) {
   if (rows_bound <= 0 || Hkv <= 0 || Hq % Hkv) return 0;
-  const Plan p = make_plan(rows_bound, Hq, Hkv, bs, max_blocks * bs);
+  const Plan p = make_plan(rows_bound, Hq, Hkv, D, bs, max_blocks * bs);
   return ws_layout(rows_bound, Hq, Hkv, D, p).total;
 }
 
@@ -680,7 +684,7 @@ int decode_rows(void *out, const void *q, const void *kc, const void *vc, const 
                 cudaStream_t st) {
   if (rows_bound <= 0) return VA_OK;
   if (rows_bound > 65535 || bs != 16) return VA_ERR_UNSUPPORTED;
-  const Plan p = make_plan(rows_bound, Hq, Hkv, bs, max_blocks * bs);
+  const Plan p = make_plan(rows_bound, Hq, Hkv, D, bs, max_blocks * bs);
   const WsLayout w = ws_layout(rows_bound, Hq, Hkv, D, p);
   if (w.total && (!ws || ws_bytes < w.total)) return VA_ERR_WORKSPACE;
   DecodeArgs a{};
@@ -724,7 +728,7 @@ extern "C" size_t va_paged_decode_workspace_size(int64_t num_seqs, int num_query
                                                  int block_size, int64_t max_seq_len) {
   if (num_seqs <= 0 || num_kv_heads <= 0 || num_query_heads % num_kv_heads || block_size <= 0)
     return 0;
-  const Plan p = make_plan(num_seqs, num_query_heads, num_kv_heads, block_size, max_seq_len);
+  const Plan p = make_plan(num_seqs, num_query_heads, num_kv_heads, head_size, block_size, max_seq_len);
   return ws_layout(num_seqs, num_query_heads, num_kv_heads, head_size, p).total;
 }
 
@@ -758,7 +762,7 @@ extern "C" int va_paged_decode(void *out, const void *q, void *k_cache, void *v_
                 !m8(new_s_head)))
     return VA_ERR_INVALID_ARG;
 
-  const Plan p = make_plan(num_seqs, num_query_heads, num_kv_heads, block_size, max_seq_len);
+  const Plan p = make_plan(num_seqs, num_query_heads, num_kv_heads, head_size, block_size, max_seq_len);
   const WsLayout w = ws_layout(num_seqs, num_query_heads, num_kv_heads, head_size, p);
   if (w.total && (!workspace || workspace_bytes < w.total)) return VA_ERR_WORKSPACE;
 

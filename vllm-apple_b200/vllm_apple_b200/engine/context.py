@@ -255,3 +255,49 @@ class EngineStepContext:
 
     def get_profiling_stats(self) -> dict:
         return {"dispatches": self._num_dispatches, "barriers": self._num_barriers}
+
+
+class CapturedStep:
+    """A step's encoded ops recorded once into a CUDA graph and replayed.
+
+    ``encode(step_ctx)`` must encode the ops of one step against FIXED buffers
+    (the graph replays the same pointers); to run the next step, copy its
+    inputs into those buffers and call :meth:`replay`.  The first call runs
+    ``encode`` eagerly ``warmup`` times (kernel attributes, workspaces and the
+    error word are set up outside the capture), then captures it.  This removes
+    the per-layer host encode cost the reference pays on every step
+    (vllm_apple/engine/runner.py:829-1176 re-encodes each step).
+    """
+
+    def __init__(self, context: EngineContext, encode, warmup: int = 1):
+        self._context = context
+        self._encode = encode
+        self._graph: Optional[torch.cuda.CUDAGraph] = None
+        self._warmup = warmup
+
+    def _run_eager(self):
+        with EngineStepContext(self._context) as sc:
+            self._encode(sc)
+
+    def capture(self) -> None:
+        stream = torch.cuda.Stream(self._context.device)
+        stream.wait_stream(self._context.stream)
+        saved = self._context.stream
+        try:
+            self._context.stream = stream
+            with torch.cuda.stream(stream):
+                for _ in range(self._warmup):
+                    self._run_eager()
+                stream.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    self._run_eager()
+            self._graph = g
+        finally:
+            self._context.stream = saved
+        self._context.stream.wait_stream(stream)
+
+    def replay(self) -> None:
+        if self._graph is None:
+            self.capture()
+        self._graph.replay()
