@@ -20,6 +20,8 @@
 #include <math.h>
 
 #include "common.cuh"
+#include <cudaTypedefs.h>
+
 #include "prefill_tc.cuh"
 
 namespace va_internal {  // split-KV decode of one-token rows (paged_decode.cu)
@@ -430,7 +432,8 @@ int launch_g(int gc, const PrefillArgs &a, dim3 grid, cudaStream_t st) {
 }
 
 template <int D, int GC>
-int launch_tc_t(const tc::Args &a, dim3 grid, cudaStream_t st) {
+int launch_tc_t(const tc::Args &a, const CUtensorMap &mk, const CUtensorMap &mv, dim3 grid,
+                cudaStream_t st) {
   using S = tc::Smem<D>;
   static int configured[64] = {0};
   int dev = 0;
@@ -442,23 +445,68 @@ int launch_tc_t(const tc::Args &a, dim3 grid, cudaStream_t st) {
       return VA_ERR_LAUNCH;
     configured[dev] = 1;
   }
-  tc::paged_prefill_tc_kernel<D, GC><<<grid, tc::kThreads, S::kBytes, st>>>(a);
+  tc::paged_prefill_tc_kernel<D, GC><<<grid, tc::kThreads, S::kBytes, st>>>(a, mk, mv);
   return va_host::launch_status();
 }
 
 template <int D>
-int launch_tc_g(int gc, const tc::Args &a, dim3 grid, cudaStream_t st) {
+int launch_tc_g(int gc, const tc::Args &a, const CUtensorMap &mk, const CUtensorMap &mv,
+                dim3 grid, cudaStream_t st) {
   switch (gc) {
-    case 1: return launch_tc_t<D, 1>(a, grid, st);
-    case 2: return launch_tc_t<D, 2>(a, grid, st);
-    case 3: return launch_tc_t<D, 3>(a, grid, st);
-    case 4: return launch_tc_t<D, 4>(a, grid, st);
-    case 5: return launch_tc_t<D, 5>(a, grid, st);
-    case 6: return launch_tc_t<D, 6>(a, grid, st);
-    case 7: return launch_tc_t<D, 7>(a, grid, st);
-    case 8: return launch_tc_t<D, 8>(a, grid, st);
+    case 1: return launch_tc_t<D, 1>(a, mk, mv, grid, st);
+    case 2: return launch_tc_t<D, 2>(a, mk, mv, grid, st);
+    case 3: return launch_tc_t<D, 3>(a, mk, mv, grid, st);
+    case 4: return launch_tc_t<D, 4>(a, mk, mv, grid, st);
+    case 5: return launch_tc_t<D, 5>(a, mk, mv, grid, st);
+    case 6: return launch_tc_t<D, 6>(a, mk, mv, grid, st);
+    case 7: return launch_tc_t<D, 7>(a, mk, mv, grid, st);
+    case 8: return launch_tc_t<D, 8>(a, mk, mv, grid, st);
   }
   return VA_ERR_UNSUPPORTED;
+}
+
+// Cache layout the TMA path understands: 0 = [nb, H, bs, D], 1 = [nb, bs, H, D], -1 = other.
+int tma_layout(int64_t sb, int64_t sh, int64_t st, int H, int bs, int D) {
+  if (sb == (int64_t)H * bs * D && sh == (int64_t)bs * D && st == D) return 0;
+  if (sb == (int64_t)bs * H * D && st == (int64_t)H * D && sh == D) return 1;
+  return -1;
+}
+
+// 3-D tensor map over one cache tensor whose box is one page x 64 head dims,
+// 128-byte swizzled.  The encoder comes from the driver through the runtime.
+bool encode_page_map(CUtensorMap *m, const void *base, int nhd, int64_t nb, int H, int bs,
+                     int D) {
+  static PFN_cuTensorMapEncodeTiled_v12000 enc = nullptr;
+  if (!enc) {
+    cudaDriverEntryPointQueryResult q;
+    void *fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return false;
+    enc = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3], estr[3] = {1, 1, 1};
+  dims[0] = (cuuint64_t)D;
+  if (nhd) {  // (D, H, nb*bs): one head, bs token rows
+    dims[1] = (cuuint64_t)H;
+    dims[2] = (cuuint64_t)(nb * bs);
+    strides[0] = (cuuint64_t)D * 2;
+    strides[1] = (cuuint64_t)H * D * 2;
+    box[0] = 64; box[1] = 1; box[2] = (cuuint32_t)bs;
+  } else {  // (D, bs, nb*H): one (block, head) page
+    dims[1] = (cuuint64_t)bs;
+    dims[2] = (cuuint64_t)(nb * H);
+    strides[0] = (cuuint64_t)D * 2;
+    strides[1] = (cuuint64_t)bs * D * 2;
+    box[0] = 64; box[1] = (cuuint32_t)bs; box[2] = 1;
+  }
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
 }
 
 int group_chunk(int g) {
@@ -487,21 +535,26 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 struct PrefillPlan {
   int TQ, gc;
   bool tc, route;
-  int64_t mt;
+  int64_t mt, rows_bound;
   size_t o_tiles, o_singles, o_dec, dec_bytes, total;
 };
 
-PrefillPlan prefill_plan(int64_t T, int64_t S, int Hq, int Hkv, int D, int bs, int64_t maxb) {
+// `tc_layout` >= 0 when the tcgen05/TMA tile kernel can take this cache.  Buffer
+// sizes use the smaller tile (more tiles) so they do not depend on the choice.
+PrefillPlan prefill_plan(int64_t T, int64_t S, int Hq, int Hkv, int D, int bs, int64_t maxb,
+                         int tc_layout) {
   PrefillPlan p{};
   p.gc = group_chunk(Hq / Hkv);
-  p.tc = use_tc_kernel(D);
+  p.tc = use_tc_kernel(D) && bs >= 8 && tc_layout >= 0;
   p.TQ = (p.tc ? tc::kRows : kRows) / p.gc;
   p.mt = max_tiles_for(T, S, p.TQ);
-  p.route = bs == 16 && p.mt <= 65535;
+  const int64_t bound = max_tiles_for(T, S, kRows / p.gc);
+  p.route = bs == 16 && bound <= 65535;
+  p.rows_bound = bound;
   p.o_tiles = 256;
-  p.o_singles = p.o_tiles + align256((size_t)p.mt * sizeof(int2));
-  p.o_dec = p.o_singles + align256((size_t)p.mt * sizeof(int32_t));
-  p.dec_bytes = p.route ? va_internal::decode_rows_workspace(p.mt, Hq, Hkv, D, bs, maxb) : 0;
+  p.o_singles = p.o_tiles + align256((size_t)bound * sizeof(int2));
+  p.o_dec = p.o_singles + align256((size_t)bound * sizeof(int32_t));
+  p.dec_bytes = p.route ? va_internal::decode_rows_workspace(bound, Hq, Hkv, D, bs, maxb) : 0;
   p.total = p.o_dec + p.dec_bytes;
   return p;
 }
@@ -516,7 +569,7 @@ extern "C" size_t va_paged_prefill_workspace_size(int64_t num_tokens, int64_t nu
       num_query_heads % num_kv_heads)
     return 0;
   return prefill_plan(num_tokens, num_seqs, num_query_heads, num_kv_heads, head_size,
-                      block_size, max_blocks_per_seq)
+                      block_size, max_blocks_per_seq, 0)
       .total;
 }
 
@@ -546,8 +599,9 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
       !va_host::aligned16(out) || !m8(s_block) || !m8(s_head) || !m8(s_token) ||
       !m8(q_s_token) || !m8(q_s_head) || o_s_token % 2 || o_s_head % 2)
     return VA_ERR_INVALID_ARG;
+  const int layout = tma_layout(s_block, s_head, s_token, num_kv_heads, block_size, head_size);
   const PrefillPlan pl = prefill_plan(num_tokens, num_seqs, num_query_heads, num_kv_heads,
-                                      head_size, block_size, max_blocks_per_seq);
+                                      head_size, block_size, max_blocks_per_seq, layout);
   if (!workspace || workspace_bytes < pl.total) return VA_ERR_WORKSPACE;
   const int G = num_query_heads / num_kv_heads;
   const int gc = pl.gc;
@@ -568,7 +622,8 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
   if (va_host::launch_status() != VA_OK) return VA_ERR_LAUNCH;
   if (pl.route) {
     const int rc = va_internal::decode_rows(
-        out, q, k_cache, v_cache, block_table, singles, singles_n, token_to_seq, positions, mt,
+        out, q, k_cache, v_cache, block_table, singles, singles_n, token_to_seq, positions,
+        pl.rows_bound,
         num_seqs, num_query_heads, num_kv_heads, head_size, block_size, max_blocks_per_seq,
         num_blocks, scale, s_block, s_head, s_token, q_s_token, q_s_head, o_s_token, o_s_head,
         ws + pl.o_dec, pl.dec_bytes, err_flag, st);
@@ -608,10 +663,16 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
     t.num_seqs = a.num_seqs; t.max_blocks = a.max_blocks; t.num_blocks = a.num_blocks;
     t.Hq = a.Hq; t.Hkv = a.Hkv; t.G = a.G; t.hgroups = a.hgroups; t.TQ = a.TQ; t.bs = a.bs;
     t.skip_singles = a.skip_singles;
+    t.nhd = layout;
     t.scale_log2 = a.scale_log2; t.s_block = a.s_block; t.s_head = a.s_head;
     t.s_token = a.s_token; t.q_s_token = a.q_s_token; t.q_s_head = a.q_s_head;
     t.o_s_token = a.o_s_token; t.o_s_head = a.o_s_head;
-    return head_size == 64 ? launch_tc_g<64>(gc, t, grid, st) : launch_tc_g<128>(gc, t, grid, st);
+    CUtensorMap mk, mv;
+    if (!encode_page_map(&mk, k_cache, layout, num_blocks, num_kv_heads, block_size, head_size) ||
+        !encode_page_map(&mv, v_cache, layout, num_blocks, num_kv_heads, block_size, head_size))
+      return VA_ERR_LAUNCH;
+    return head_size == 64 ? launch_tc_g<64>(gc, t, mk, mv, grid, st)
+                           : launch_tc_g<128>(gc, t, mk, mv, grid, st);
   }
   switch (head_size) {
     case 32: return launch_g<32>(gc, a, grid, st);
