@@ -43,15 +43,21 @@ constexpr int kKeys = 64;   // keys per staged chunk (4 pages of 16)
 constexpr int kThreads = 128;
 
 // ---------------------------------------------------------------------------
-// planner: tiles[i] = {first token, token count}; tiles_n = number of tiles
+// planner: tiles[i] = {first token, token count}; tiles_n = number of tiles;
+// optionally order[] = tile indices by descending context of their last token
+// (counting sort over 64-key buckets), so the longest tiles launch first.
 // ---------------------------------------------------------------------------
+constexpr int kOrderBuckets = 2048;
+
 __global__ void __launch_bounds__(1024) plan_tiles_kernel(const int32_t *token_to_seq,
+                                                          const int32_t *positions,
                                                           int64_t T, int TQ, int2 *tiles,
                                                           int32_t *tiles_n, int64_t max_tiles,
                                                           int32_t *singles, int32_t *singles_n,
-                                                          int32_t *err) {
+                                                          int32_t *order, int32_t *err) {
   __shared__ int warp_buf[32];
   __shared__ int carry_max, carry_sum, n_single;
+  __shared__ int bucket[kOrderBuckets];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   if (tid == 0) { carry_max = 0; carry_sum = 0; n_single = 0; }
   __syncthreads();
@@ -124,6 +130,44 @@ __global__ void __launch_bounds__(1024) plan_tiles_kernel(const int32_t *token_t
     *tiles_n = n;
     if (singles_n) *singles_n = n_single;
   }
+  if (!order) return;
+  // bucket b holds tiles whose last token sees about 64 * (kOrderBuckets - 1 - b) keys
+  auto bucket_of = [&](int i) {
+    const int2 t = tiles[i];
+    const int p = positions[t.x + t.y - 1];
+    const int w = (p < 0 || (singles && t.y == 1)) ? 0 : (p >> 6) + 1;
+    return kOrderBuckets - 1 - min(w, kOrderBuckets - 1);
+  };
+  for (int b = tid; b < kOrderBuckets; b += 1024) bucket[b] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += 1024) atomicAdd(&bucket[bucket_of(i)], 1);
+  __syncthreads();
+  // exclusive scan of the bucket counts (two buckets per thread)
+  {
+    const int b0 = 2 * tid;
+    const int c0 = bucket[b0], c1 = bucket[b0 + 1];
+    int x = c0 + c1;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_buf[wid] = x;
+    __syncthreads();
+    if (wid == 0) {
+      int w = warp_buf[lane];
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += y;
+      }
+      warp_buf[lane] = w;
+    }
+    __syncthreads();
+    const int excl = x - (c0 + c1) + (wid > 0 ? warp_buf[wid - 1] : 0);
+    bucket[b0] = excl;
+    bucket[b0 + 1] = excl + c0;
+  }
+  __syncthreads();
+  for (int i = tid; i < n; i += 1024) order[atomicAdd(&bucket[bucket_of(i)], 1)] = i;
 }
 
 // ---------------------------------------------------------------------------
@@ -536,7 +580,7 @@ struct PrefillPlan {
   int TQ, gc;
   bool tc, route;
   int64_t mt, rows_bound;
-  size_t o_tiles, o_singles, o_dec, dec_bytes, total;
+  size_t o_tiles, o_singles, o_order, o_dec, dec_bytes, total;
 };
 
 // `tc_layout` >= 0 when the tcgen05/TMA tile kernel can take this cache.  Buffer
@@ -546,14 +590,16 @@ PrefillPlan prefill_plan(int64_t T, int64_t S, int Hq, int Hkv, int D, int bs, i
   PrefillPlan p{};
   p.gc = group_chunk(Hq / Hkv);
   p.tc = use_tc_kernel(D) && bs >= 8 && tc_layout >= 0;
-  p.TQ = (p.tc ? tc::kRows : kRows) / p.gc;
+  // the tcgen05 kernel takes a pair of tiles of kRows / gc tokens per CTA
+  p.TQ = p.tc ? tc::kTiles * (tc::kRows / p.gc) : kRows / p.gc;
   p.mt = max_tiles_for(T, S, p.TQ);
   const int64_t bound = max_tiles_for(T, S, kRows / p.gc);
   p.route = bs == 16 && bound <= 65535;
   p.rows_bound = bound;
   p.o_tiles = 256;
   p.o_singles = p.o_tiles + align256((size_t)bound * sizeof(int2));
-  p.o_dec = p.o_singles + align256((size_t)bound * sizeof(int32_t));
+  p.o_order = p.o_singles + align256((size_t)bound * sizeof(int32_t));
+  p.o_dec = p.o_order + align256((size_t)bound * sizeof(int32_t));
   p.dec_bytes = p.route ? va_internal::decode_rows_workspace(bound, Hq, Hkv, D, bs, maxb) : 0;
   p.total = p.o_dec + p.dec_bytes;
   return p;
@@ -599,7 +645,10 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
       !va_host::aligned16(out) || !m8(s_block) || !m8(s_head) || !m8(s_token) ||
       !m8(q_s_token) || !m8(q_s_head) || o_s_token % 2 || o_s_head % 2)
     return VA_ERR_INVALID_ARG;
-  const int layout = tma_layout(s_block, s_head, s_token, num_kv_heads, block_size, head_size);
+  // the tensor-core kernel folds the scale into its exponent and needs it > 0
+  const int layout = scale > 0.f
+                         ? tma_layout(s_block, s_head, s_token, num_kv_heads, block_size, head_size)
+                         : -1;
   const PrefillPlan pl = prefill_plan(num_tokens, num_seqs, num_query_heads, num_kv_heads,
                                       head_size, block_size, max_blocks_per_seq, layout);
   if (!workspace || workspace_bytes < pl.total) return VA_ERR_WORKSPACE;
@@ -616,9 +665,11 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
   int2 *tiles = reinterpret_cast<int2 *>(ws + pl.o_tiles);
   int32_t *singles = reinterpret_cast<int32_t *>(ws + pl.o_singles);
   auto st = static_cast<cudaStream_t>(stream);
-  plan_tiles_kernel<<<1, 1024, 0, st>>>(token_to_seq, num_tokens, TQ, tiles, tiles_n, mt,
-                                        pl.route ? singles : nullptr,
-                                        pl.route ? singles_n : nullptr, err_flag);
+  int32_t *order = reinterpret_cast<int32_t *>(ws + pl.o_order);
+  plan_tiles_kernel<<<1, 1024, 0, st>>>(token_to_seq, positions, num_tokens, TQ, tiles, tiles_n,
+                                        mt, pl.route ? singles : nullptr,
+                                        pl.route ? singles_n : nullptr,
+                                        use_tc ? order : nullptr, err_flag);
   if (va_host::launch_status() != VA_OK) return VA_ERR_LAUNCH;
   if (pl.route) {
     const int rc = va_internal::decode_rows(
@@ -659,9 +710,10 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
   if (use_tc) {
     tc::Args t{};
     t.out = a.out; t.q = a.q; t.kc = a.kc; t.vc = a.vc; t.bt = a.bt; t.tok_seq = a.tok_seq;
-    t.pos = a.pos; t.tiles = a.tiles; t.tiles_n = a.tiles_n; t.err = a.err;
+    t.pos = a.pos; t.tiles = a.tiles; t.order = order; t.tiles_n = a.tiles_n; t.err = a.err;
     t.num_seqs = a.num_seqs; t.max_blocks = a.max_blocks; t.num_blocks = a.num_blocks;
-    t.Hq = a.Hq; t.Hkv = a.Hkv; t.G = a.G; t.hgroups = a.hgroups; t.TQ = a.TQ; t.bs = a.bs;
+    t.Hq = a.Hq; t.Hkv = a.Hkv; t.G = a.G; t.hgroups = a.hgroups; t.TQ = a.TQ / tc::kTiles;
+    t.bs = a.bs;
     t.skip_singles = a.skip_singles;
     t.nhd = layout;
     t.scale_log2 = a.scale_log2; t.s_block = a.s_block; t.s_head = a.s_head;
@@ -671,8 +723,12 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
     if (!encode_page_map(&mk, k_cache, layout, num_blocks, num_kv_heads, block_size, head_size) ||
         !encode_page_map(&mv, v_cache, layout, num_blocks, num_kv_heads, block_size, head_size))
       return VA_ERR_LAUNCH;
-    return head_size == 64 ? launch_tc_g<64>(gc, t, mk, mv, grid, st)
-                           : launch_tc_g<128>(gc, t, mk, mv, grid, st);
+    // one dimension, tile-major: blocks launch in the planner's longest-first order
+    const int64_t nblk = mt * (int64_t)grid.y;
+    if (nblk > INT32_MAX) return VA_ERR_UNSUPPORTED;
+    const dim3 grid1((unsigned)nblk);
+    return head_size == 64 ? launch_tc_g<64>(gc, t, mk, mv, grid1, st)
+                           : launch_tc_g<128>(gc, t, mk, mv, grid1, st);
   }
   switch (head_size) {
     case 32: return launch_g<32>(gc, a, grid, st);

@@ -2,30 +2,35 @@
 // (tcgen05 UMMA, TMEM accumulators), head_size 64 or 128.  Included by
 // paged_prefill.cu, which owns the tile planner and the C-ABI entry point.
 //
-// One CTA (4 warps, 128 threads) per (tile, kv head [, q-head group]):
-//   * 128 MMA rows = (token, q head) pairs of up to 128/G consecutive tokens of
-//     one sequence, so each staged K/V chunk serves every head of the group;
-//     thread t owns row t (TMEM lane t) for the whole softmax.
-//   * Q, K and V tiles live in shared memory in the 128-byte-swizzled
-//     canonical layout (8-row x 128-byte atoms).  K and V chunks of 64 keys
-//     arrive by TMA (cp.async.bulk.tensor.3d, one box per page and 64 head
-//     dims, hardware 128-byte swizzle, no multicast), issued by one thread and
-//     completed on a per-stage mbarrier, kStages deep (chunk j+3 is requested
-//     as soon as chunk j-1 retires).  Invalid pages and pages past the context
-//     are zero-filled by the threads; V rows past the context in the last page
-//     are zeroed after their page lands.  Q is staged once by cp.async.
-//   * S = Q K^T (M=128, N=64, K=D) goes to one of two TMEM buffers, so the MMA
-//     of chunk j+1 runs while the rows of chunk j are in softmax; O (M=128,
-//     N=D) accumulates in TMEM: rows whose running max grew are rescaled in
-//     TMEM before the next PV MMA.  P (fp16) is written to shared memory in
-//     the same swizzled layout and consumed by O += P V (V as an MN-major
-//     operand: the same shared-memory image as K).
-//   * Warp roles: one producer warp runs ahead of the math, fetching block ids
-//     and issuing the TMA boxes of chunk c into stage c % kStages as soon as
-//     the tensor core has finished with that stage (a tcgen05.commit after the
-//     chunk's PV MMA arrives on the stage's "empty" barrier); eight softmax
-//     warps own the rows, and one of their threads issues every MMA.  Every
-//     wait on an mbarrier is bounded and reports VA_FLAG_WAIT_TIMEOUT.
+// One CTA per (tile pair, kv head [, q-head group]); 11 warps with fixed roles.
+// CTAs are launched longest context first (the planner orders the tiles), so
+// the long tiles of every sequence and head start in the first wave.
+//   * A tile = 128 MMA rows = (token, q head) pairs of up to 128/G consecutive
+//     tokens of one sequence; a CTA owns two consecutive tiles of the same
+//     sequence, so every staged K/V chunk serves both tiles and every head of
+//     the group.  Warpgroup h (warps 4h..4h+3) runs the softmax of tile h, one
+//     thread per row (TMEM lane = row).
+//   * Warp 8 (producer) streams K and V in chunks of 64 keys by TMA
+//     (cp.async.bulk.tensor.3d, one box per page and 64 head dims, hardware
+//     128-byte swizzle, no multicast) into kStages stages; a stage is reused
+//     once the tensor core has finished with it (tcgen05.commit on the
+//     stage's "empty" barrier).  Block ids are read a warp-group of pages
+//     ahead; invalid pages and pages past the context are zero-filled, and
+//     the page holding the end of the context is copied row by row with its
+//     tail zeroed (V rows past the context must not hold NaN: P = 0 there).
+//   * Warp 9 + h (MMA for tile h) issues S_h = Q_h K^T (M=128, N=64, K=D) two
+//     chunks ahead into one of two TMEM buffers, and O_h += P_h V (V as an
+//     MN-major operand: the same shared-memory image as K) once warpgroup h
+//     has published P_h.  One issuing warp per tile: neither tile waits for
+//     the other's softmax; a stage is free when both warps committed it.
+//   * Softmax: log2-domain online softmax; the max only moves when it grows by
+//     more than 2^8, so O is rarely rescaled in TMEM.  P (fp16) goes to shared
+//     memory in the swizzled K-major layout.
+//   * Q is staged once by cp.async from the softmax and MMA warps, while the
+//     producer already streams the first chunks.
+//   * Every wait on an mbarrier is bounded and reports VA_FLAG_WAIT_TIMEOUT;
+//     after a timeout the CTA runs to the end without waiting or issuing,
+//     waits (bounded) for its copies and MMAs in flight and frees TMEM.
 #pragma once
 
 #include <cuda.h>
@@ -36,9 +41,12 @@ namespace tc {
 
 constexpr int kRows = 128;  // MMA M
 constexpr int kKeys = 64;   // keys per chunk (MMA N of S, MMA K of PV)
-constexpr int kConsumers = 256;          // 8 softmax warps: two threads per MMA row
-constexpr int kThreads = kConsumers + 32;  // + 1 producer warp (TMA)
-constexpr uint32_t kTmemCols = 256;  // S x2 (2 x 64) + O (<= 128)
+constexpr int kTiles = 2;   // tiles (softmax warpgroups) per CTA
+constexpr int kSoftmax = kTiles * kRows;  // softmax threads, one per row
+constexpr int kProducerWarp = kSoftmax / 32, kMmaWarp = kProducerWarp + 1;  // MMA: 9, 10
+constexpr int kMath = kSoftmax + 32 * kTiles;  // softmax + MMA threads
+constexpr int kThreads = kMath + 32;           // + producer warp
+constexpr uint32_t kTmemCols = 512;  // S: 2 tiles x 2 buffers x 64; O: 2 tiles x D (<= 128)
 constexpr uint32_t kWaitLimit = 1u << 22;
 constexpr int kStages = 4;  // K/V chunks in flight (a chunk = 64 keys of K and of V)
 
@@ -152,10 +160,13 @@ struct Args {
   const __half *q, *kc, *vc;
   const int32_t *bt, *tok_seq, *pos;
   const int2 *tiles;
+  const int32_t *order;  // tile indices, longest context first
   const int32_t *tiles_n;
   int32_t *err;
   int64_t num_seqs, max_blocks, num_blocks;
-  int Hq, Hkv, G, hgroups, TQ, bs, skip_singles;
+  int Hq, Hkv, G, hgroups;
+  int TQ;  // tokens per tile (a CTA owns up to 2 * TQ)
+  int bs, skip_singles;
   int nhd;  // cache layout of the tensor maps: 0 = [nb, H, bs, D], 1 = [nb, bs, H, D]
   float scale_log2;
   int64_t s_block, s_head, s_token, q_s_token, q_s_head, o_s_token, o_s_head;
@@ -163,57 +174,63 @@ struct Args {
 
 template <int D>
 struct Smem {
-  static constexpr uint32_t kQ = kRows * D * 2;    // 16/32 KB
-  static constexpr uint32_t kKV = kKeys * D * 2;   // 8/16 KB per chunk
-  static constexpr uint32_t kP = kRows * kKeys * 2;  // 16 KB
-  static constexpr uint32_t oQ = 0, oK = kQ, oV = oK + kStages * kKV, oP = oV + kStages * kKV;
-  static constexpr uint32_t oBar = oP + kP;  // S, PV, full[kStages], empty[kStages] + tmem slot
-  // + slack to align the base to 1 KB; D=64 is padded so at most 2 CTAs share
-  // an SM (2 x 256 TMEM columns = the whole TMEM)
-  static constexpr uint32_t kNeed = oBar + 128 + 1024;
-  static constexpr uint32_t kBytes = (D == 64 && kNeed < 80u * 1024) ? 80u * 1024 : kNeed;
+  static constexpr uint32_t kQ = kRows * D * 2;      // 16/32 KB per tile
+  static constexpr uint32_t kKV = kKeys * D * 2;     // 8/16 KB per chunk
+  static constexpr uint32_t kP = kRows * kKeys * 2;  // 16 KB per tile
+  static constexpr uint32_t oQ = 0, oK = kTiles * kQ, oV = oK + kStages * kKV,
+                            oP = oV + kStages * kKV;
+  static constexpr uint32_t oBar = oP + kTiles * kP;  // mbarriers + tmem slot
+  static constexpr uint32_t oPos = oBar + 256;        // int [kTiles][kRows]
+  static constexpr uint32_t kBytes = oPos + kTiles * kRows * 4 + 1024;  // + 1 KB alignment slack
 };
 
-// Named barrier over the 8 softmax warps only (the producer warp runs free).
-VA_DEVINL void consumer_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
-}
+// Named barrier over the softmax and MMA warps (the producer warp runs free).
+VA_DEVINL void math_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kMath) : "memory"); }
+// Every warp of the CTA, met from different places in the role code.
+VA_DEVINL void all_sync() { asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory"); }
 
 template <int D, int GC>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 1)
     paged_prefill_tc_kernel(const Args a, const __grid_constant__ CUtensorMap tmk,
                             const __grid_constant__ CUtensorMap tmv) {
   using S = Smem<D>;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   // 128-byte swizzle atoms must sit on 1024-byte boundaries of the shared window
   unsigned char *smem = smem_raw + ((1024u - (va::smem_addr(smem_raw) & 1023u)) & 1023u);
-  uint64_t *bar_s = reinterpret_cast<uint64_t *>(smem + S::oBar);
-  uint64_t *bar_pv = bar_s + 1;
-  uint64_t *bar_full = bar_s + 2;              // [kStages]: chunk landed
-  uint64_t *bar_empty = bar_full + kStages;    // [kStages]: tensor core done with the stage
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_empty + kStages);
-  __shared__ int s_pos[kRows];
-  __shared__ float s_red[2][kRows];  // per-half row max (per chunk) / row sum (at the end)
-  __shared__ int s_ctx, s_bad_from, s_dead;
+  uint64_t *bar_full = reinterpret_cast<uint64_t *>(smem + S::oBar);  // [kStages] chunk landed
+  uint64_t *bar_empty = bar_full + kStages;  // [kStages] both MMA warps done with the stage
+  uint64_t *bar_s = bar_empty + kStages;     // [kTiles][2] S buffer written
+  uint64_t *bar_p = bar_s + 2 * kTiles;      // [kTiles] P published (kRows arrivals)
+  uint64_t *bar_pv = bar_p + kTiles;         // [kTiles] PV done
+  uint64_t *bar_done = bar_pv + kTiles;      // [kTiles] every MMA of the tile retired
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_done + kTiles);
+  int *s_pos = reinterpret_cast<int *>(smem + S::oPos);  // [kTiles][kRows]
+  __shared__ int s_ctx[kTiles], s_bad_from, s_dead;
 
-  const int tile = blockIdx.x;
-  if (tile >= *a.tiles_n) return;
+  const int ny = a.Hkv * a.hgroups;
+  const int item = (int)(blockIdx.x / (unsigned)ny);
+  if (item >= *a.tiles_n) return;
+  const int tile = a.order[item];
   const int2 td = a.tiles[tile];
   const int t0 = td.x, nq = td.y;
   if (nq == 1 && a.skip_singles) return;  // handled by the split-KV decode kernel
   const int seq = a.tok_seq[t0];
-  const int kvh = blockIdx.y / a.hgroups;
-  const int hg = blockIdx.y - kvh * a.hgroups;
+  const int yb = (int)(blockIdx.x - (unsigned)item * ny);
+  const int kvh = yb / a.hgroups;
+  const int hg = yb - kvh * a.hgroups;
   const int head0 = kvh * a.G + hg * GC;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int BS = a.bs;
+  const int BS = a.bs, TQ = a.TQ;
 
-  if (tid == 0) { s_ctx = 0; s_bad_from = INT_MAX; s_dead = 0; }
+  if (tid < kTiles) s_ctx[tid] = 0;
+  if (tid == 0) { s_bad_from = INT_MAX; s_dead = 0; }
   __syncthreads();
-  if (tid < a.TQ) {
+  if (tid < kSoftmax) {
+    const int h = tid / kRows, tk = tid % kRows;
     int p = -1;
-    if (tid < nq && seq >= 0 && seq < a.num_seqs) {
-      p = a.pos[t0 + tid];
+    const int ti = h * TQ + tk;
+    if (tk < TQ && ti < nq && seq >= 0 && seq < a.num_seqs) {
+      p = a.pos[t0 + ti];
       if (p >= 0 && (int64_t)((p + BS) / BS) > a.max_blocks) {
         va::raise_flag(a.err, VA_FLAG_CTX_OVERFLOW);
         p = -1;
@@ -221,43 +238,34 @@ __global__ void __launch_bounds__(kThreads)
       if (p < 0) p = -1;
     }
     s_pos[tid] = p;
-    if (p >= 0) atomicMax(&s_ctx, p + 1);
+    if (p >= 0) atomicMax(&s_ctx[h], p + 1);
   }
-  __syncthreads();
-  const int ctx = s_ctx;
-  if (ctx == 0) return;
-  const int nch = (ctx + kKeys - 1) / kKeys;
-  const int32_t *bt_row = a.bt + (int64_t)seq * a.max_blocks;
-
-  // ---- barriers + TMEM ----
   if (tid == 0) {
-    va::mbar_init(bar_s, 1);
-    va::mbar_init(bar_pv, 1);
     for (int i = 0; i < kStages; ++i) {
       va::mbar_init(&bar_full[i], 1);
-      va::mbar_init(&bar_empty[i], 1);
+      va::mbar_init(&bar_empty[i], kTiles);
+    }
+    for (int i = 0; i < 2 * kTiles; ++i) va::mbar_init(&bar_s[i], 1);
+    for (int i = 0; i < kTiles; ++i) {
+      va::mbar_init(&bar_p[i], kRows);
+      va::mbar_init(&bar_pv[i], 1);
+      va::mbar_init(&bar_done[i], 1);
     }
     va::fence_barrier_init();
   }
-  if (warp == 0) tmem_alloc(tmem_slot, kTmemCols);
+  if (warp == kMmaWarp) tmem_alloc(tmem_slot, kTmemCols);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
+  const int ctx = max(s_ctx[0], s_ctx[1]);
   const uint32_t tmem = *tmem_slot;
-
-  constexpr int CPR = D / 8;
-  // Q: every thread, 16-byte cp.async into the swizzled layout (once)
-  for (int i = tid; i < kRows * CPR; i += kThreads) {
-    const int r = i / CPR, c = i - r * CPR;
-    const int tk = r / GC, g = r - tk * GC;
-    unsigned char *dst = smem + S::oQ + sw128_off(r, c * 8, kRows);
-    if (tk < nq && tk < a.TQ)
-      cp_async16(dst, a.q + (int64_t)(t0 + tk) * a.q_s_token + (int64_t)(head0 + g) * a.q_s_head +
-                          c * 8);
-    else
-      *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+  if (ctx == 0) {  // nothing to attend (all tokens skipped): release TMEM and leave
+    if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+    return;
   }
-  cp_async_commit();
+  const int nch = (ctx + kKeys - 1) / kKeys;
+  const int32_t *bt_row = a.bt + (int64_t)seq * a.max_blocks;
+  constexpr int CPR = D / 8;  // 16-byte pieces per row
 
   auto dead = [&]() { return *(volatile int *)&s_dead != 0; };
   auto timeout = [&]() {
@@ -268,10 +276,11 @@ __global__ void __launch_bounds__(kThreads)
     if (!va::mbar_wait_bounded(bar, parity, kWaitLimit)) timeout();
   };
 
-  if (warp == kConsumers / 32) {
-    // =================== producer warp: TMA staging of K/V chunks ===================
+  if (warp == kProducerWarp) {
+    // =================== producer: K/V chunks into the stages ===================
     const int npc = kKeys / BS;  // a power of two <= 8: a chunk never straddles a group
     const int pages = (ctx + BS - 1) / BS;  // <= max_blocks (checked above)
+    const int tail_rows = ctx - (pages - 1) * BS;  // rows of the last page inside the context
     // block ids are read 32 pages (one per lane) at a time, one group ahead
     auto load_group = [&](int g) -> int32_t {
       const int page = g * 32 + lane;
@@ -300,25 +309,36 @@ __global__ void __launch_bounds__(kThreads)
           id = -2;
         }
       }
-      // zero the stage rows of pages that will not be loaded (past context / invalid)
       unsigned char *kb = smem + S::oK + buf * S::kKV, *vb = smem + S::oV + buf * S::kKV;
-      const unsigned valid = __ballot_sync(0xffffffffu, lane < npc && id >= 0);
-      if (valid != (1u << npc) - 1u) {  // a hole: only near the end of the context
+      // by TMA: valid whole pages; by the warp: the partial last page (copied, tail
+      // zeroed) and invalid / past-context pages (zeroed)
+      const bool part = page == pages - 1 && tail_rows < BS;
+      const unsigned valid = __ballot_sync(0xffffffffu, lane < npc && id >= 0 && !part);
+      const unsigned partial = __ballot_sync(0xffffffffu, lane < npc && id >= 0 && part);
+      if (valid != (1u << npc) - 1u) {  // only near the end of the context
+        const int ppage = partial ? __ffs(partial) - 1 : -1;
+        const int32_t pid = __shfl_sync(0xffffffffu, id, ppage < 0 ? 0 : ppage);
         for (int i = lane; i < kKeys * CPR; i += 32) {
           const int r = i / CPR, ch16 = i - r * CPR;
-          if (!((valid >> (r / BS)) & 1u)) {
-            const uint32_t o = sw128_off(r, ch16 * 8, kKeys);
-            *reinterpret_cast<uint4 *>(kb + o) = make_uint4(0, 0, 0, 0);
-            *reinterpret_cast<uint4 *>(vb + o) = make_uint4(0, 0, 0, 0);
+          const int p = r / BS;
+          if ((valid >> p) & 1u) continue;
+          const uint32_t o = sw128_off(r, ch16 * 8, kKeys);
+          uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+          if (p == ppage && r - p * BS < tail_rows) {
+            const int64_t off = (int64_t)pid * a.s_block + (int64_t)kvh * a.s_head +
+                                (int64_t)(r - p * BS) * a.s_token + ch16 * 8;
+            kv = __ldg(reinterpret_cast<const uint4 *>(a.kc + off));
+            vv = __ldg(reinterpret_cast<const uint4 *>(a.vc + off));
           }
+          *reinterpret_cast<uint4 *>(kb + o) = kv;
+          *reinterpret_cast<uint4 *>(vb + o) = vv;
         }
         va::fence_proxy_async_smem();
         __syncwarp();
       }
       if (lane == 0) va::mbar_arrive_expect_tx(&bar_full[buf], __popc(valid) * (2u * BS * D * 2u));
       __syncwarp();
-      // one box per lane: lane = (page, 64-column block, K or V)
-      {
+      {  // one box per lane: lane = (page, 64-column block, K or V)
         constexpr int kBoxes = D / 64 * 2;
         const int p = lane / kBoxes, rem = lane - p * kBoxes;
         const int kbk = rem >> 1;
@@ -336,192 +356,234 @@ __global__ void __launch_bounds__(kThreads)
       __syncwarp();
       if (dead()) break;
     }
-    // no copy may still be landing when the CTA exits (normally all have: the
-    // softmax warps consumed every chunk); bounded, reports like any other wait
+    // no copy may still be landing when the CTA exits (normally none is: the
+    // MMA warps consumed every chunk); bounded, reports like any other wait
     if (lane == 0) {
       for (int c = nch - kStages < 0 ? 0 : nch - kStages; c < nch; ++c)
-        if (!va::mbar_wait_bounded(&bar_full[c % kStages], (uint32_t)((c / kStages) & 1), kWaitLimit))
+        if (!va::mbar_wait_bounded(&bar_full[c % kStages], (uint32_t)((c / kStages) & 1),
+                                   kWaitLimit))
           timeout();
     }
     __syncwarp();
+    all_sync();
   } else {
-    // =================== softmax warps (+ MMA issue by thread 0) ===================
-    const int row = tid & (kRows - 1);
-    const int half = tid >> 7;
-    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t tO = tmem + 2 * kKeys;
-    const uint32_t sQ = va::smem_addr(smem + S::oQ);
-    const uint32_t sK = va::smem_addr(smem + S::oK);
-    const uint32_t sV = va::smem_addr(smem + S::oV);
-    const uint32_t sP = va::smem_addr(smem + S::oP);
-    constexpr uint32_t IDESC_S = idesc_f16(kRows, kKeys, false);
-    constexpr uint32_t IDESC_O = idesc_f16(kRows, D, true);
-
-    // S_j = Q K_j^T: A = Q [128 x D] K-major, B = K chunk [64 x D] K-major.
-    auto issue_s = [&](int j) {
-      if (tid == 0 && !dead()) {
-        fence_after_sync();
-        const uint32_t kbase = sK + (j % kStages) * S::kKV;
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          const uint32_t kblk = ks >> 2, kin = (ks & 3) * 32;
-          umma_f16(tmem + (j & 1) * kKeys, sdesc(sQ + kblk * kRows * 128 + kin, 16, 1024),
-                   sdesc(kbase + kblk * kKeys * 128 + kin, 16, 1024), IDESC_S, ks > 0);
-        }
-        umma_commit(bar_s);
-      }
-    };
-    // O (+)= P_j V_j: A = P [128 x 64] K-major, B = V chunk [64 keys x D] MN-major (the
-    // same swizzled image as a K tile: LBO = next 64 columns, SBO = next 8 keys); then the
-    // stage is released to the producer once both MMAs of chunk j are done.
-    auto issue_pv = [&](int j) {
-      if (tid == 0 && !dead()) {
-        fence_after_sync();
-        const uint32_t vbase = sV + (j % kStages) * S::kKV;
-#pragma unroll
-        for (int ks = 0; ks < kKeys / 16; ++ks)
-          umma_f16(tO, sdesc(sP + ks * 32, 16, 1024), sdesc(vbase + ks * 2048, kKeys * 128, 1024),
-                   IDESC_O, (j > 0 || ks > 0) ? 1u : 0u);
-        umma_commit(bar_pv);
-        umma_commit(&bar_empty[j % kStages]);
-      }
-    };
-    // chunk ch landed; V rows past the context inside the last page are zeroed
-    // (p = 0 there, but 0 * garbage could be NaN)
-    auto wait_chunk = [&](int ch) {
-      const int buf = ch % kStages;
-      wait_bar(&bar_full[buf], (uint32_t)((ch / kStages) & 1));
-      if (ch == nch - 1 && ctx % kKeys != 0) {
-        for (int i = tid; i < kKeys * CPR; i += kConsumers) {
-          const int r = i / CPR, c = i - r * CPR;
-          if (ch * kKeys + r >= ctx)
-            *reinterpret_cast<uint4 *>(smem + S::oV + buf * S::kKV + sw128_off(r, c * 8, kKeys)) =
-                make_uint4(0, 0, 0, 0);
-        }
-      }
-    };
-
+    // ---- Q of both tiles: cp.async by the softmax and MMA warps ----
+    const int mtid = warp > kProducerWarp ? tid - 32 : tid;  // 0 .. kMath - 1
+    for (int i = mtid; i < kTiles * kRows * CPR; i += kMath) {
+      const int r2 = i / CPR, c = i - r2 * CPR;
+      const int h = r2 / kRows, r = r2 - h * kRows;
+      const int tk = r / GC, g = r - tk * GC;
+      const int ti = h * TQ + tk;
+      unsigned char *dst = smem + S::oQ + h * S::kQ + sw128_off(r, c * 8, kRows);
+      if (tk < TQ && ti < nq)
+        cp_async16(dst, a.q + (int64_t)(t0 + ti) * a.q_s_token + (int64_t)(head0 + g) * a.q_s_head +
+                            c * 8);
+      else
+        *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+    }
+    cp_async_commit();
     cp_async_wait<0>();
-    wait_chunk(0);
     va::fence_proxy_async_smem();
-    consumer_sync();
-    issue_s(0);
+    math_sync();
 
-    const int tk = row / GC;
-    const int my_pos = (tk < a.TQ) ? s_pos[tk] : -1;
-    // m: the max the probabilities are taken against.  It only moves when the row
-    // max exceeds it by more than 2^8 (P stays <= 256, exact enough in fp16, and
-    // O / l at the end cancels it), so O is rescaled in TMEM rarely.
-    float m = -INFINITY, l = 0.f;  // l: this thread's half of the row sum
-
+    if (warp > kProducerWarp) {
+      // =================== MMA issue for tile h (lane 0) ===================
+      const int h = warp - kMmaWarp;
+      const int nj = (s_ctx[h] + kKeys - 1) / kKeys;
+      const uint32_t sQ = va::smem_addr(smem + S::oQ) + h * S::kQ;
+      const uint32_t sK = va::smem_addr(smem + S::oK);
+      const uint32_t sV = va::smem_addr(smem + S::oV);
+      const uint32_t sP = va::smem_addr(smem + S::oP) + h * S::kP;
+      const uint32_t tS = tmem + 2 * h * kKeys;        // two S buffers of this tile
+      const uint32_t tO = tmem + 4 * kKeys + h * D;    // O of this tile
+      constexpr uint32_t IDESC_S = idesc_f16(kRows, kKeys, false);
+      constexpr uint32_t IDESC_O = idesc_f16(kRows, D, true);
+      auto wait_chunk = [&](int c) {
+        wait_bar(&bar_full[c % kStages], (uint32_t)((c / kStages) & 1));
+      };
+      // S_h(j) = Q_h K_j^T: A = Q_h [128 x D] K-major, B = K chunk [64 x D] K-major.
+      auto issue_s = [&](int j) {
+        if (lane == 0 && !dead()) {
+          fence_after_sync();
+          const uint32_t kbase = sK + (j % kStages) * S::kKV;
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const uint32_t kblk = ks >> 2, kin = (ks & 3) * 32;
+            umma_f16(tS + (j & 1) * kKeys, sdesc(sQ + kblk * kRows * 128 + kin, 16, 1024),
+                     sdesc(kbase + kblk * kKeys * 128 + kin, 16, 1024), IDESC_S, ks > 0);
+          }
+          umma_commit(&bar_s[2 * h + (j & 1)]);
+        }
+        __syncwarp();
+      };
+      // O_h (+)= P_h V_j: A = P_h [128 x 64] K-major, B = V chunk [64 keys x D] MN-major
+      // (LBO = next 64 columns, SBO = next 8 keys).
+      auto issue_pv = [&](int j) {
+        wait_bar(&bar_p[h], (uint32_t)(j & 1));
+        if (lane == 0 && !dead()) {
+          fence_after_sync();
+          const uint32_t vbase = sV + (j % kStages) * S::kKV;
+#pragma unroll
+          for (int ks = 0; ks < kKeys / 16; ++ks)
+            umma_f16(tO, sdesc(sP + ks * 32, 16, 1024),
+                     sdesc(vbase + ks * 2048, kKeys * 128, 1024), IDESC_O,
+                     (j > 0 || ks > 0) ? 1u : 0u);
+          umma_commit(&bar_pv[h]);
+        }
+        __syncwarp();
+      };
+      // S runs two chunks ahead of PV: S_h(j+2) reuses the buffer of S_h(j), read
+      // before P_h(j) was published.  Every chunk is waited for (and released) by
+      // both MMA warps, also past this tile's context, so the stage barriers stay
+      // in step.
 #pragma unroll 1
-    for (int j = 0; j < nch; ++j) {
-      // (1) this thread's 32 scores of chunk j, masked, and their max
-      wait_bar(bar_s, (uint32_t)(j & 1));
-      fence_after_sync();
-      uint32_t sr[32];
-      tmem_ld32(tmem + (j & 1) * kKeys + half * 32 + lane_base, sr);
-      tmem_wait_ld();
-      fence_before_sync();
-      float p[32];
-      const int kbase = j * kKeys + half * 32;
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float s = __uint_as_float(sr[c]) * a.scale_log2;
-        p[c] = (kbase + c <= my_pos) ? s : -INFINITY;
-        mx4[c & 3] = fmaxf(mx4[c & 3], p[c]);
+      for (int c = 0; c < 2 && c < nch; ++c) {
+        wait_chunk(c);
+        if (c < nj) issue_s(c);
       }
-      s_red[half][row] = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-      // (2) chunk j+1 landed -> (3) S_{j+1} on the tensor core
-      if (j + 1 < nch) wait_chunk(j + 1);
-      va::fence_proxy_async_smem();
-      consumer_sync();
-      if (j + 1 < nch) issue_s(j + 1);
-      // (4) online softmax against the (lazily moved) max of both halves of the row
-      const float rmax = fmaxf(s_red[0][row], s_red[1][row]);
-      const float mn = (m == -INFINITY || rmax > m + 8.f) ? fmaxf(m, rmax) : m;
-      const bool none = mn == -INFINITY;
-      const float alpha = (none || mn == m) ? 1.f : va::fast_exp2(m - mn);
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        p[c] = none ? 0.f : va::fast_exp2(p[c] - mn);
-        sum4[c & 3] += p[c];
+#pragma unroll 1
+      for (int j = 0; j < nch; ++j) {
+        if (j < nj) issue_pv(j);
+        if (j + 2 < nch) {
+          wait_chunk(j + 2);
+          if (j + 2 < nj) issue_s(j + 2);
+        }
+        if (lane == 0 && !dead()) umma_commit(&bar_empty[j % kStages]);
+        __syncwarp();
       }
-      l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-      m = mn;
-      // (5) PV_{j-1} done: P buffer and O are free
-      if (j > 0) {
-        wait_bar(bar_pv, (uint32_t)((j - 1) & 1));
+      // teardown: every MMA issued by this thread has retired
+      if (lane == 0) {
+        umma_commit(&bar_done[h]);
+        if (!va::mbar_wait_bounded(&bar_done[h], 0, kWaitLimit)) timeout();
+      }
+      __syncwarp();
+      all_sync();
+    } else {
+      // =================== softmax of tile h, one thread per row ===================
+      const int h = warp >> 2;
+      const int row = tid & (kRows - 1);
+      const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+      const uint32_t tO = tmem + 4 * kKeys + h * D + lane_base;
+      const int tk = row / GC;
+      const int my_pos = (tk < TQ) ? s_pos[h * kRows + tk] : -1;
+      const int nj = (s_ctx[h] + kKeys - 1) / kKeys;
+      unsigned char *prow = smem + S::oP + h * S::kP;
+      // m: the max the probabilities are taken against.  It only moves when the row
+      // max exceeds it by more than 2^8 (P stays <= 256, exact enough in fp16, and
+      // O / l at the end cancels it), so O is rescaled in TMEM rarely.
+      float m = -INFINITY, l = 0.f;
+#pragma unroll 1
+      for (int j = 0; j < nj; ++j) {
+        wait_bar(&bar_s[2 * h + (j & 1)], (uint32_t)((j >> 1) & 1));
         fence_after_sync();
-      }
-      // (6) rescale this thread's half of O where the max moved (warp-collective)
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-#pragma unroll 1
-        for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
-          uint32_t o[32];
-          tmem_ld32(tO + lane_base + c, o);
+        float p[kKeys];
+        {
+          uint32_t sr[32];
+          const uint32_t tS = tmem + (2 * h + (j & 1)) * kKeys + lane_base;
+          tmem_ld32(tS, sr);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tO + lane_base + c, o);
+          for (int c = 0; c < 32; ++c) p[c] = __uint_as_float(sr[c]);
+          tmem_ld32(tS + 32, sr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) p[32 + c] = __uint_as_float(sr[c]);
         }
-        tmem_wait_st();
-      }
-      // (7) this thread's 32 probabilities -> P (fp16, swizzled)
+        // raw scores: the scale (> 0) is applied in the exponent's FMA
+        const int vis = my_pos - j * kKeys;  // keys 0..vis of this chunk are visible
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (vis < kKeys - 1) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint4 w;
-        w.x = va::pack_h2(p[8 * c + 0], p[8 * c + 1]);
-        w.y = va::pack_h2(p[8 * c + 2], p[8 * c + 3]);
-        w.z = va::pack_h2(p[8 * c + 4], p[8 * c + 5]);
-        w.w = va::pack_h2(p[8 * c + 6], p[8 * c + 7]);
-        *reinterpret_cast<uint4 *>(smem + S::oP + sw128_off(row, half * 32 + c * 8, kRows)) = w;
-      }
-      va::fence_proxy_async_smem();
-      fence_before_sync();
-      consumer_sync();
-      issue_pv(j);
-    }
-
-    // ---- epilogue: O / l -> fp16 rows ----
-    wait_bar(bar_pv, (uint32_t)((nch - 1) & 1));
-    s_red[half][row] = l;
-    consumer_sync();
-    const bool ok = !dead();  // uniform across the softmax warps after the barrier
-    const float lt = s_red[0][row] + s_red[1][row];
-    const int bad_from = s_bad_from;
-    if (bad_from != INT_MAX && tid == 0) va::raise_flag(a.err, VA_FLAG_BAD_BLOCK);
-    const bool write = ok && my_pos >= 0 && my_pos < bad_from && tk < nq && row < a.TQ * GC;
-    const float inv = lt > 0.f ? 1.f / lt : 0.f;
-    const int g = row - tk * GC;
-    __half *orow = a.out + (int64_t)(t0 + tk) * a.o_s_token + (int64_t)(head0 + g) * a.o_s_head;
-    if (ok) {
-      fence_after_sync();
+          for (int c = 0; c < kKeys; ++c) p[c] = c <= vis ? p[c] : -INFINITY;
+        }
+#pragma unroll
+        for (int c = 0; c < kKeys; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], p[c]);
+        const float rmax =
+            fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
+        const float mn = (m == -INFINITY || rmax > m + 8.f) ? fmaxf(m, rmax) : m;
+        const bool none = mn == -INFINITY;
+        const float alpha = (none || mn == m) ? 1.f : va::fast_exp2(m - mn);
+        const float nmn = none ? 0.f : -mn;
+        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < kKeys; ++c) {
+          p[c] = va::fast_exp2(fmaf(p[c], a.scale_log2, nmn));
+          sum4[c & 3] += p[c];
+        }
+        l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+        m = mn;
+        // PV_h(j-1) done: P_h and O_h are free
+        if (j > 0) {
+          wait_bar(&bar_pv[h], (uint32_t)((j - 1) & 1));
+          fence_after_sync();
+        }
+        // rescale this row of O where the max moved (warp-collective TMEM access)
+        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-      for (int c = half * (D / 2); c < (half + 1) * (D / 2); c += 32) {
-        uint32_t o[32];
-        tmem_ld32(tO + lane_base + c, o);
-        tmem_wait_ld();
-        if (write) {
+          for (int c = 0; c < D; c += 32) {
+            uint32_t o[32];
+            tmem_ld32(tO + c, o);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 w;
-            w.x = va::pack_h2(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
-            w.y = va::pack_h2(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
-            w.z = va::pack_h2(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
-            w.w = va::pack_h2(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
-            *reinterpret_cast<uint4 *>(orow + c + i) = w;
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + c, o);
+          }
+          tmem_wait_st();
+        }
+        // P row (fp16, swizzled), then publish it to the MMA warp
+#pragma unroll
+        for (int c = 0; c < kKeys / 8; ++c) {
+          uint4 w;
+          w.x = va::pack_h2(p[8 * c + 0], p[8 * c + 1]);
+          w.y = va::pack_h2(p[8 * c + 2], p[8 * c + 3]);
+          w.z = va::pack_h2(p[8 * c + 4], p[8 * c + 5]);
+          w.w = va::pack_h2(p[8 * c + 6], p[8 * c + 7]);
+          *reinterpret_cast<uint4 *>(prow + sw128_off(row, c * 8, kRows)) = w;
+        }
+        va::fence_proxy_async_smem();
+        fence_before_sync();
+        va::mbar_arrive(&bar_p[h]);
+      }
+      if (nj > 0) {
+        wait_bar(&bar_pv[h], (uint32_t)((nj - 1) & 1));
+        fence_after_sync();
+      }
+      // ---- epilogue: O / l -> fp16 rows, once every role is done ----
+      all_sync();  // s_bad_from / s_dead are final
+      const bool ok = !dead();  // uniform across the CTA after the barrier
+      const int bad_from = s_bad_from;
+      if (bad_from != INT_MAX && tid == 0) va::raise_flag(a.err, VA_FLAG_BAD_BLOCK);
+      const int ti = h * TQ + tk;
+      const bool write = ok && nj > 0 && my_pos >= 0 && my_pos < bad_from && tk < TQ && ti < nq &&
+                         row < TQ * GC;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int g = row - tk * GC;
+      __half *orow = a.out + (int64_t)(t0 + ti) * a.o_s_token + (int64_t)(head0 + g) * a.o_s_head;
+      if (ok && nj > 0) {
+#pragma unroll 1
+        for (int c = 0; c < D; c += 32) {
+          uint32_t o[32];
+          tmem_ld32(tO + c, o);
+          tmem_wait_ld();
+          if (write) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 w;
+              w.x = va::pack_h2(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
+              w.y = va::pack_h2(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+              w.z = va::pack_h2(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+              w.w = va::pack_h2(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+              *reinterpret_cast<uint4 *>(orow + c + i) = w;
+            }
           }
         }
       }
     }
   }
-  // producer and softmax warps meet here; warp 0 releases TMEM
+  // all roles meet here; the first MMA warp releases TMEM
   fence_before_sync();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     fence_after_sync();
     tmem_dealloc(tmem, kTmemCols);
   }
