@@ -130,6 +130,61 @@ VA_DEVINL void tma_load_3d(void *dst, const CUtensorMap *map, int c0, int c1, in
       : "memory");
 }
 
+// ---- packed fp32 pairs (sm_100 f32x2 arithmetic) -----------------------------
+VA_DEVINL uint64_t pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+VA_DEVINL void upk2(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+VA_DEVINL uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+VA_DEVINL uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+VA_DEVINL uint64_t fsub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+VA_DEVINL float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// 2^x for a pair, x <= ~8, on the FMA pipe instead of the special-function
+// unit: x = n + f with n = round(x) (add/subtract 1.5 * 2^23), f in [-1/2, 1/2];
+// 2^f by a cubic fitted here for minimal relative error on [-1/2, 1/2]
+// (max relative error 7.6e-5, below fp16's half ulp 4.9e-4); 2^n enters as an
+// exponent-field add.  x is clamped to -126, where the result is below 2^-125
+// (the hardware path returns 0 there): both round to 0 in fp16.
+VA_DEVINL uint64_t exp2_poly2(uint64_t x) {
+  float a, b;
+  upk2(x, a, b);
+  x = pk2(fmaxf(a, -126.f), fmaxf(b, -126.f));
+  const uint64_t M = pk2(12582912.f, 12582912.f);
+  const uint64_t t = fadd2(x, M);
+  const uint64_t f = fsub2(x, fsub2(t, M));
+  uint64_t y = ffma2(pk2(0.05517050251364708f, 0.05517050251364708f), f,
+                     pk2(0.24260824918746948f, 0.24260824918746948f));
+  y = ffma2(y, f, pk2(0.693260908126831f, 0.693260908126831f));
+  y = ffma2(y, f, pk2(0.9999282360076904f, 0.9999282360076904f));
+  float y0, y1, t0, t1;
+  upk2(y, y0, y1);
+  upk2(t, t0, t1);
+  // low bits of t hold n (two's complement); n << 23 lands in the exponent field
+  y0 = __uint_as_float(__float_as_uint(y0) + (__float_as_uint(t0) << 23));
+  y1 = __uint_as_float(__float_as_uint(y1) + (__float_as_uint(t1) << 23));
+  return pk2(y0, y1);
+}
+
 // ---- descriptors ------------------------------------------------------------
 // Shared-memory matrix descriptor, 128-byte swizzle (canonical 8-row x 128 B
 // atoms, atoms 1024-byte aligned).  lbo/sbo in bytes.
@@ -474,10 +529,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       float m = -INFINITY, l = 0.f;
 #pragma unroll 1
       for (int j = 0; j < nj; ++j) {
-        wait_bar(&bar_s[2 * h + (j & 1)], (uint32_t)((j >> 1) & 1));
-        fence_after_sync();
         float p[kKeys];
         {
+          wait_bar(&bar_s[2 * h + (j & 1)], (uint32_t)((j >> 1) & 1));
+          fence_after_sync();
           uint32_t sr[32];
           const uint32_t tS = tmem + (2 * h + (j & 1)) * kKeys + lane_base;
           tmem_ld32(tS, sr);
@@ -489,29 +544,52 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < 32; ++c) p[32 + c] = __uint_as_float(sr[c]);
         }
-        // raw scores: the scale (> 0) is applied in the exponent's FMA
-        const int vis = my_pos - j * kKeys;  // keys 0..vis of this chunk are visible
-        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        if (vis < kKeys - 1) {
+        float alpha;
+        {
+          // raw scores: the scale (> 0) is applied in the exponent's FMA
+          const int vis = my_pos - j * kKeys;  // keys 0..vis of this chunk are visible
+          if (vis < kKeys - 1) {
 #pragma unroll
-          for (int c = 0; c < kKeys; ++c) p[c] = c <= vis ? p[c] : -INFINITY;
+            for (int c = 0; c < kKeys; ++c) p[c] = c <= vis ? p[c] : -INFINITY;
+          }
+          float mx4[4] = {p[0], p[1], p[2], p[3]};
+#pragma unroll
+          for (int c = 4; c < kKeys; c += 8) {
+            mx4[0] = fmax3(mx4[0], p[c + 0], p[c + 1]);
+            mx4[1] = fmax3(mx4[1], p[c + 2], p[c + 3]);
+            mx4[2] = fmax3(mx4[2], p[c + 4], p[c + 5]);
+            if (c + 7 < kKeys) mx4[3] = fmax3(mx4[3], p[c + 6], p[c + 7]);
+            else mx4[3] = fmaxf(mx4[3], p[c + 6]);
+          }
+          const float rmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
+          const float mn = (m == -INFINITY || rmax > m + 8.f) ? fmaxf(m, rmax) : m;
+          const bool none = mn == -INFINITY;
+          alpha = (none || mn == m) ? 1.f : va::fast_exp2(m - mn);
+          const float nmn = none ? 0.f : -mn;
+          // p = 2^(s * scale - m) in pairs; every third pair on the FMA pipe (the
+          // special-function unit is the softmax's bottleneck)
+          const uint64_t sc2 = pk2(a.scale_log2, a.scale_log2), nm2 = pk2(nmn, nmn);
+          uint64_t sum2[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)};
+#pragma unroll
+          for (int c = 0; c < kKeys / 2; ++c) {
+            const uint64_t x = ffma2(pk2(p[2 * c], p[2 * c + 1]), sc2, nm2);
+            uint64_t e;
+            if (c % 3 == 2) {
+              e = exp2_poly2(x);
+            } else {
+              float x0, x1;
+              upk2(x, x0, x1);
+              e = pk2(va::fast_exp2(x0), va::fast_exp2(x1));
+            }
+            upk2(e, p[2 * c], p[2 * c + 1]);
+            sum2[c & 1] = fadd2(sum2[c & 1], e);
+          }
+          float s0, s1, s2, s3;
+          upk2(sum2[0], s0, s1);
+          upk2(sum2[1], s2, s3);
+          l = l * alpha + ((s0 + s1) + (s2 + s3));
+          m = mn;
         }
-#pragma unroll
-        for (int c = 0; c < kKeys; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], p[c]);
-        const float rmax =
-            fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
-        const float mn = (m == -INFINITY || rmax > m + 8.f) ? fmaxf(m, rmax) : m;
-        const bool none = mn == -INFINITY;
-        const float alpha = (none || mn == m) ? 1.f : va::fast_exp2(m - mn);
-        const float nmn = none ? 0.f : -mn;
-        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int c = 0; c < kKeys; ++c) {
-          p[c] = va::fast_exp2(fmaf(p[c], a.scale_log2, nmn));
-          sum4[c & 3] += p[c];
-        }
-        l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-        m = mn;
         // PV_h(j-1) done: P_h and O_h are free
         if (j > 0) {
           wait_bar(&bar_pv[h], (uint32_t)((j - 1) & 1));
