@@ -280,6 +280,15 @@ VA_API int va_rope(void *q, void *k, const float *cos_cache, const float *sin_ca
 VA_API int va_silu_mul(void *out, const void *gate, const void *up, int64_t num_elements,
                 void *stream);
 
+/* Top-k logits per token: indices[T][k] (int32) and values[T][k] (fp16), largest
+ * first, ties by the lower index.  logits is fp16 [T][row_stride] (row_stride >=
+ * vocab_size elements).  NaN and -inf are never selected; rows with fewer than
+ * k other logits are padded with index -1 and value -inf.  1 <= k <= 1024.
+ * Replaces EngineTopK.encode -- topk_select / topk_select_small_k
+ * (vllm_apple/engine/ops/topk.py:57-283, :317-399). */
+VA_API int va_topk(int32_t *indices, void *values, const void *logits, int64_t num_tokens,
+                   int64_t vocab_size, int64_t row_stride, int k, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

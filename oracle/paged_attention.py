@@ -380,3 +380,78 @@ def kv_sync_blocks(src_k, src_v, dst_k, dst_v, block_table, seq_lens, src_layout
                 _row(dst_k, dst_layout, b, hh, t)[...] = _row(src_k, src_layout, b, hh, t)
                 _row(dst_v, dst_layout, b, hh, t)[...] = _row(src_v, src_layout, b, hh, t)
     return dst_k, dst_v
+
+
+# --------------------------------------------------------------------------
+# top-k logits
+# --------------------------------------------------------------------------
+
+
+def _topk_keys(bits: np.ndarray) -> np.ndarray:
+    """Order-preserving integer key of fp16 bit patterns; 0 for NaN and -inf."""
+    b = bits.astype(np.int64)
+    key = np.where(b & 0x8000, (~b) & 0xFFFF, b | 0x8000)
+    bad = ((b & 0x7FFF) > 0x7C00) | (b == 0xFC00)
+    return np.where(bad, 0, key)
+
+
+def topk(logits, k):
+    """Top-k per row of fp16 ``logits [T, V]`` -> (int32 indices, fp16 values), each
+    ``[T, k]``, largest first.
+
+    Follows EngineTopK's selection (vllm_apple/engine/ops/topk.py:80-151, the
+    insertion list of the k best values initialised to -inf, and its merge
+    :153-216): a logit is kept only if it is greater than -inf (so NaN and -inf never
+    are), rows with fewer than k kept logits are padded with index -1 and value
+    -inf (the list's initial entries, written out at :218-226).  Order between equal
+    values is by the lower index, and +0 ranks above -0 (the bit-level order);
+    the reference leaves both to its thread layout.
+    """
+    x = np.ascontiguousarray(np.asarray(logits, dtype=np.float16))
+    T, V = x.shape
+    keys = _topk_keys(x.view(np.uint16))
+    idx = np.full((T, k), -1, dtype=np.int32)
+    val = np.full((T, k), -np.inf, dtype=np.float16)
+    cols = np.arange(V)
+    for t in range(T):
+        order = np.lexsort((cols, -keys[t]))  # key desc, index asc
+        order = order[keys[t][order] > 0][:k]
+        idx[t, :len(order)] = order
+        val[t, :len(order)] = x[t, order]
+    return idx, val
+
+
+def topk_insertion_lists(logits, k, threads=64):
+    """Pure-Python restatement of the reference kernel's own two stages (per-thread
+    insertion lists over a strided slice of the row, then a pairwise tree merge,
+    vllm_apple/engine/ops/topk.py:80-216) for small cases; returns the values in
+    the reference's output order (used to pin ``topk`` by value)."""
+    x = np.asarray(logits, dtype=np.float16)
+    T, V = x.shape
+    out_v = np.full((T, k), -np.inf, dtype=np.float32)
+    out_i = np.full((T, k), -1, dtype=np.int64)
+
+    def insert(vals, idxs, v, i):
+        if v > vals[k - 1]:
+            pos = next(j for j in range(k) if v > vals[j])
+            vals.insert(pos, v)
+            idxs.insert(pos, i)
+            del vals[k:], idxs[k:]
+
+    for t in range(T):
+        lists = []
+        for th in range(threads):
+            vals, idxs = [-np.inf] * k, [-1] * k
+            for i in range(th, V, threads):
+                insert(vals, idxs, float(x[t, i]), i)
+            lists.append((vals, idxs))
+        stride = threads // 2
+        while stride > 0:
+            for th in range(stride):
+                vals, idxs = lists[th]
+                ov, oi = lists[th + stride]
+                for v, i in zip(ov, oi):
+                    insert(vals, idxs, v, i)
+            stride //= 2
+        out_v[t], out_i[t] = lists[0][0], lists[0][1]
+    return out_i, out_v.astype(np.float16)

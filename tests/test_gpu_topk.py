@@ -1,0 +1,96 @@
+"""Top-k logits on the GPU vs the oracle: indices and values bit-exact."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import paged_attention as ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from vllm_apple_b200 import ops
+    return ops
+
+
+def _logits(seed, T, V, special):
+    g = torch.Generator().manual_seed(seed)
+    x = (torch.randn(T, V, generator=g) * 3).half()
+    if special:
+        x[0, torch.randint(0, V, (7,), generator=g)] = float("nan")
+        x[0, torch.randint(0, V, (7,), generator=g)] = float("-inf")
+        x[0, torch.randint(0, V, (2,), generator=g)] = float("inf")
+        if T > 1:
+            x[1] = 0.25                                  # one long tie
+        if T > 2:
+            x[2, : V // 2] = float("-inf")               # few valid logits
+            x[2, V // 2:] = float("nan")
+            x[2, V - 1] = -0.0
+            x[2, V - 2] = 0.0
+    return x
+
+
+def _check(x, k, stride=None):
+    ops = _ops()
+    T, V = x.shape
+    if stride is None:
+        dx = x.cuda()
+    else:
+        buf = torch.full((T, stride), float("nan"), dtype=torch.float16)
+        buf[:, :V] = x
+        dx = buf.cuda()[:, :V]
+    idx = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    val = torch.empty(T, k, dtype=torch.float16, device="cuda")
+    ops.topk(idx, val, dx, k)
+    ei, ev = ref.topk(x.numpy(), k)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ei)
+    np.testing.assert_array_equal(val.cpu().view(torch.int16).numpy(), ev.view(np.int16))
+
+
+@pytest.mark.parametrize("T,V,k", [(64, 32000, 50), (8, 151936, 8), (3, 131072, 1024),
+                                   (5, 1000, 1), (4, 7, 3), (2, 9, 16), (300, 4096, 64)])
+@pytest.mark.parametrize("special", [False, True])
+def test_topk(T, V, k, special):
+    _check(_logits(T * 7 + V + k, T, V, special), k)
+
+
+@pytest.mark.parametrize("stride", [32003, 32008])
+def test_topk_row_stride(stride):
+    _check(_logits(stride, 6, 32000, True), 40, stride=stride)
+
+
+def test_topk_fp16_range_extremes():
+    x = torch.tensor([[65504.0, -65504.0, 6e-8, -6e-8, 0.0, -0.0, 1.0, 1.0]]).half()
+    _check(x, 8)
+    _check(x, 3)
+
+
+def test_topk_engine_op():
+    from vllm_apple_b200.engine import EngineContext, EngineTopK
+    ctx = EngineContext()
+    op = EngineTopK(ctx, k=50)
+    assert op.k == 50 and op.get_stats() == {"k": 50}
+    x = _logits(1, 16, 32000, False)
+    dx = x.cuda()
+    idx = torch.empty(16, 50, dtype=torch.int32, device="cuda")
+    val = torch.empty(16, 50, dtype=torch.float16, device="cuda")
+    with ctx.new_step() as sc:
+        op.encode(sc, dx, idx, val, 16, 32000)
+        sc.submit()
+        sc.wait_until_completed()
+    ei, ev = ref.topk(x.numpy(), 50)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ei)
+    np.testing.assert_array_equal(val.cpu().numpy(), ev)
+
+
+def test_topk_rejects():
+    from vllm_apple_b200 import _lib
+    lib = _lib.load()
+    x = torch.zeros(2, 100, dtype=torch.float16, device="cuda")
+    i = torch.empty(2, 2048, dtype=torch.int32, device="cuda")
+    v = torch.empty(2, 2048, dtype=torch.float16, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    assert lib.va_topk(i.data_ptr(), v.data_ptr(), x.data_ptr(), 2, 100, 100, 0, s) == 1
+    assert lib.va_topk(i.data_ptr(), v.data_ptr(), x.data_ptr(), 2, 100, 99, 5, s) == 1
+    assert lib.va_topk(i.data_ptr(), v.data_ptr(), x.data_ptr(), 2, 100, 100, 1025, s) == 2
+    assert lib.va_topk(i.data_ptr(), v.data_ptr(), x.data_ptr(), 0, 100, 100, 5, s) == 0

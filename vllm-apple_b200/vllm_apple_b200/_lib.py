@@ -72,6 +72,7 @@ SIGNATURES = {
     "va_rope": (c_int, [P, P, P, P, P, I64, c_int, c_int, c_int, c_int, I64, I64, I64, c_int, P,
                         P]),
     "va_silu_mul": (c_int, [P, P, P, I64, P]),
+    "va_topk": (c_int, [P, P, P, I64, I64, I64, c_int, P]),
 }
 
 _lib = None

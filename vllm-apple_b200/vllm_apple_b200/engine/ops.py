@@ -342,3 +342,45 @@ class EngineElementwiseOps:
         _lib.check(_lib.load().va_silu_mul(resolve(output)[0], resolve(gate)[0], resolve(up)[0],
                                            num_elements, step_ctx.stream_handle), "va_silu_mul")
         step_ctx.note_dispatch()
+
+
+TOPK_K_ENV = "VLLM_METAL_TOPK_K"
+
+
+class EngineTopK:
+    """Top-k logits per token on the device, so sampling reads back k (index, value)
+    pairs instead of the whole vocabulary row.
+
+    Mirrors ``EngineTopK`` (vllm_apple/engine/ops/topk.py:40-412): same constructor
+    (``k`` defaults to 50, ``VLLM_METAL_TOPK_K`` overrides it), same ``encode``
+    signature and outputs (int32 indices and fp16 values, ``[num_tokens, k]``,
+    largest first).  The selection runs in ``va_topk`` for any 1 <= k <= 1024.
+    """
+
+    def __init__(self, context: Any, k: int = 50):
+        import os
+        self._context = context
+        self._k = k
+        env_k = os.environ.get(TOPK_K_ENV)
+        if env_k:
+            try:
+                self._k = int(env_k)
+            except ValueError:
+                pass
+        _lib.load()
+
+    def encode(self, step_ctx, logits, indices_out, values_out, num_tokens: int,
+               vocab_size: int, k: Optional[int] = None) -> None:
+        step_ctx.require_encoding("encode()")
+        k = k or self._k
+        _lib.check(_lib.load().va_topk(resolve(indices_out)[0], resolve(values_out)[0],
+                                       resolve(logits)[0], num_tokens, vocab_size, vocab_size, k,
+                                       step_ctx.stream_handle), "va_topk")
+        step_ctx.note_dispatch()
+
+    @property
+    def k(self) -> int:
+        return self._k
+
+    def get_stats(self) -> Dict[str, Any]:
+        return {"k": self._k}

@@ -301,6 +301,27 @@ def silu_mul(out, gate, up, num_elements=None):
                                        _stream(dev)), "va_silu_mul")
 
 
+def topk(indices, values, logits, k, num_tokens=None):
+    """Top-k of each row of fp16 ``logits [T, V]`` (row stride may exceed V):
+    ``indices [T, k]`` int32 and ``values [T, k]`` fp16, largest first, ties by the
+    lower index; NaN / -inf are never selected and short rows are padded with
+    (-1, -inf)."""
+    dev = _dev_index(logits)
+    if logits.dtype != torch.float16 or logits.dim() != 2 or logits.stride(1) != 1:
+        raise TypeError("logits must be a float16 [T, V] tensor with unit inner stride")
+    if indices.dtype != torch.int32 or values.dtype != torch.float16:
+        raise TypeError("indices must be int32 and values float16")
+    for t, n in ((indices, "indices"), (values, "values")):
+        if not t.is_contiguous():
+            raise TypeError(f"{n} must be contiguous")
+    T = logits.shape[0] if num_tokens is None else num_tokens
+    if indices.numel() < T * k or values.numel() < T * k:
+        raise ValueError("indices / values hold fewer than num_tokens * k entries")
+    _lib.check(_lib.load().va_topk(indices.data_ptr(), values.data_ptr(), logits.data_ptr(), T,
+                                   logits.shape[1], logits.stride(0), int(k), _stream(dev)),
+               "va_topk")
+
+
 # ---------------------------------------------------------------------------
 # step-level ops
 # ---------------------------------------------------------------------------

@@ -106,10 +106,22 @@ def run_elementwise(which, iters, warmup):
         _report("silu_mul", sec, 3 * e.gate.numel() * 2, shape=list(e.gate.shape))
 
 
+def run_topk(iters, warmup):
+    """Top-k over a decode batch's logits: 1024 rows x 131072 vocab (268 MB, above
+    L2), k = 50 (the reference's default)."""
+    g = torch.Generator().manual_seed(0)
+    T, V, k = 1024, 131072, 50
+    x = (torch.randn(T, V, generator=g) * 3).half().cuda()
+    idx = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    val = torch.empty(T, k, dtype=torch.float16, device="cuda")
+    sec = _time(lambda: ops.topk(idx, val, x, k), iters, warmup)
+    _report("topk", sec, T * V * 2 + T * k * 6, shape=[T, V], k=k)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", default="all",
-                    choices=["decode", "mixed", "rmsnorm", "rope", "silu_mul", "all"])
+                    choices=["decode", "mixed", "rmsnorm", "rope", "silu_mul", "topk", "all"])
     ap.add_argument("--workload", default="devstral_b128")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
@@ -121,6 +133,8 @@ def main():
         run_mixed(a.iters, a.warmup)
     if a.op in ("rmsnorm", "rope", "silu_mul", "all"):
         run_elementwise(a.op, a.iters, a.warmup)
+    if a.op in ("topk", "all"):
+        run_topk(a.iters, a.warmup)
 
 
 if __name__ == "__main__":
