@@ -9,14 +9,23 @@
 // -inf.  Ties are resolved by the lower index (the reference's order between
 // equal values depends on its thread layout; values are identical either way).
 //
-// Design (HBM-bound: one read of the row from DRAM, two more from L2): one CTA
-// per row runs a 16-bit radix select on an order-preserving key of the fp16
-// bits -- a 256-bin histogram of the high byte (per-warp private bins), the
-// bin holding the k-th largest, a 256-bin histogram of the low byte inside
-// that bin -- which yields the exact k-th key.  A third pass compacts the keys
-// above it (any order) and the lowest-index ties equal to it (block-wide
-// ordered scan), then a shared-memory bitonic sort orders the <= 1024
-// candidates by (key desc, index asc).
+// Design (HBM-bound: one read of the row from DRAM, a second from L2), one CTA
+// per row, on an order-preserving 16-bit key of the fp16 bits:
+//   * fast path (k <= 512): every thread takes the max of its slice (fp16 max
+//     over 16-byte vectors); the k-th largest of those maxima -- found by a
+//     binary search over the key bits with block-wide counts -- is a lower
+//     bound of the row's k-th largest key (the k maxima above it are k
+//     distinct logits), so the logits at or above it contain the answer, ties
+//     included.  A second pass screens 8 logits at a time with an fp16 compare
+//     against the bound and appends the few that pass to shared memory
+//     (warp-aggregated slots); the list is sorted by (key desc, index asc)
+//     with a bitonic sort and the first k written.
+//   * exact path (k > 512, fewer than k threads holding a valid logit, or more
+//     than kCap logits passing the bound, e.g. a row of equal logits): a radix
+//     select -- 256-bin histograms of the high, then the low byte (per-warp
+//     private bins) -- finds the exact k-th key; the keys above it (any order)
+//     and the lowest-index ties equal to it (block-wide ordered scan) are
+//     compacted and sorted the same way.
 #include "common.cuh"
 #include "vllm_apple_b200.h"
 
@@ -25,6 +34,7 @@ namespace {
 constexpr int kThreads = 512;
 constexpr int kWarps = kThreads / 32;
 constexpr int kMaxK = 1024;
+constexpr int kCap = 2048;  // candidates of the fast path
 
 // Order-preserving 16-bit key of an fp16 bit pattern, 0 for NaN and -inf
 // (never selected).  Valid keys lie in [0x0400, 0xFC00].
@@ -43,20 +53,92 @@ VA_DEVINL void for_each(const uint16_t *row, int64_t n, bool vec, F &&f) {
   const int tid = threadIdx.x;
   int64_t done = 0;
   if (vec) {
+    constexpr int kU = 4;  // independent 16-byte loads in flight per thread
     const int64_t nv = n / 8;
     const uint4 *rv = reinterpret_cast<const uint4 *>(row);
-    for (int64_t i = tid; i < nv; i += kThreads) {
-      const uint4 v = __ldg(rv + i);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    for (int64_t i0 = tid; i0 < nv; i0 += (int64_t)kThreads * kU) {
+      uint4 v[kU];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        f(i * 8 + 2 * j, w[j] & 0xFFFFu);
-        f(i * 8 + 2 * j + 1, w[j] >> 16);
+      for (int u = 0; u < kU; ++u) {
+        const int64_t i = i0 + (int64_t)u * kThreads;
+        if (i < nv) v[u] = __ldg(rv + i);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t i = i0 + (int64_t)u * kThreads;
+        if (i >= nv) continue;
+        const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          f(i * 8 + 2 * j, w[j] & 0xFFFFu);
+          f(i * 8 + 2 * j + 1, w[j] >> 16);
+        }
       }
     }
     done = nv * 8;
   }
   for (int64_t i = done + tid; i < n; i += kThreads) f(i, (uint32_t)__ldg(row + i));
+}
+
+// Calls f8(first index, 8 fp16 as uint4) for the 16-byte vectors of an aligned
+// row (kU loads in flight per thread) and f1(index, fp16 bits) for the
+// remaining elements.
+template <typename F8, typename F1>
+VA_DEVINL void for_each8(const uint16_t *row, int64_t n, bool vec, F8 &&f8, F1 &&f1) {
+  const int tid = threadIdx.x;
+  int64_t done = 0;
+  if (vec) {
+    constexpr int kU = 4;
+    const int64_t nv = n / 8;
+    const uint4 *rv = reinterpret_cast<const uint4 *>(row);
+    for (int64_t i0 = tid; i0 < nv; i0 += (int64_t)kThreads * kU) {
+      uint4 v[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t i = i0 + (int64_t)u * kThreads;
+        if (i < nv) v[u] = __ldg(rv + i);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int64_t i = i0 + (int64_t)u * kThreads;
+        if (i < nv) f8(i * 8, v[u]);
+      }
+    }
+    done = nv * 8;
+  }
+  for (int64_t i = done + tid; i < n; i += kThreads) f1(i, (uint32_t)__ldg(row + i));
+}
+
+VA_DEVINL __half2 as_h2(uint32_t w) { return *reinterpret_cast<__half2 *>(&w); }
+VA_DEVINL uint32_t as_u32(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+// Bitonic sort of cand[0, m) (m a power of two), descending, by the block or
+// (WARP) by warp 0 alone.
+template <bool WARP>
+VA_DEVINL void sort_desc(unsigned long long *cand, int m) {
+  const int t = WARP ? (threadIdx.x & 31) : threadIdx.x;
+  const int nt = WARP ? 32 : kThreads;
+  for (int size = 2; size <= m; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = t; i < m / 2; i += nt) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool desc = (lo & size) == 0;
+        const unsigned long long a = cand[lo], b = cand[hi];
+        if ((a < b) == desc) {
+          cand[lo] = b;
+          cand[hi] = a;
+        }
+      }
+      if (WARP) __syncwarp(); else __syncthreads();
+    }
+  }
+}
+
+// Candidate: key in the high word, complemented index in the low word, so that
+// the descending order is (key desc, index asc); 0 = empty.
+VA_DEVINL unsigned long long pack_cand(uint32_t key, int64_t i) {
+  return ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)i);
 }
 
 // Block-wide exclusive scan of one int per thread; returns the exclusive
@@ -123,17 +205,106 @@ VA_DEVINL int radix_step(const uint16_t *row, int64_t n, bool vec, int shift, ui
   return total;
 }
 
-__global__ void __launch_bounds__(kThreads) topk_kernel(int32_t *out_idx, uint16_t *out_val,
+__global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uint16_t *out_val,
                                                         const uint16_t *logits, int64_t n,
                                                         int64_t row_stride, int k, int vec) {
   __shared__ int whist[kWarps][256];
   __shared__ int hist[256];
   __shared__ int warp_sums[kWarps];
   __shared__ int s_bin, s_above, s_gt, s_ties;
-  __shared__ unsigned long long cand[kMaxK];
-  const int tid = threadIdx.x;
+  __shared__ unsigned long long cand[kCap];
+  __shared__ int s_cnt;
+  const int tid = threadIdx.x, lane = tid & 31;
   const uint16_t *row = logits + (int64_t)blockIdx.x * row_stride;
   const bool v = vec != 0;
+
+  // ---- fast path: bound from the per-thread maxima, screen, sort ----
+  if (k <= kThreads) {
+    // fp16 max of the vectors (NaN ignored; whether -0 or +0 wins a tie only
+    // lowers the bound, which stays valid), keys for the rest
+    uint32_t mx = 0;
+    __half2 m2 = as_h2(0xFC00FC00u);  // (-inf, -inf)
+    for_each8(
+        row, n, v,
+        [&](int64_t, const uint4 &q) {
+          m2 = __hmax2(m2, __hmax2(__hmax2(as_h2(q.x), as_h2(q.y)), __hmax2(as_h2(q.z), as_h2(q.w))));
+        },
+        [&](int64_t, uint32_t h) { mx = max(mx, key_of(h)); });
+    mx = max(mx, max(key_of(as_u32(m2) & 0xFFFFu), key_of(as_u32(m2) >> 16)));
+    if (tid == 0) s_cnt = 0;
+    // the k-th largest thread max = the largest x with #(maxima >= x) >= k
+    uint32_t bound = 0;
+#pragma unroll 1
+    for (int bit = 15; bit >= 0; --bit) {
+      const uint32_t x = bound | (1u << bit);
+      if (__syncthreads_count(mx >= x) >= k) bound = x;
+    }
+    if (bound != 0u) {  // at least k valid logits: the answer is inside the bound
+      // screen 8 at a time against the bound's value (a superset of the keys >=
+      // bound: -0 and +0 compare equal), then one warp round per pending logit
+      const __half2 b2 = as_h2(half_bits_of(bound) * 0x10001u);
+      auto append = [&](unsigned act, uint32_t pend, const uint32_t (&w)[4], int64_t i0) {
+        while (__any_sync(act, pend != 0u)) {
+          const bool take = pend != 0u;
+          const int j = __ffs(pend) - 1;
+          pend &= pend - 1u;
+          const unsigned ball = __ballot_sync(act, take);
+          const int leader = __ffs(ball) - 1;
+          int base = 0;
+          if (lane == leader) base = atomicAdd(&s_cnt, __popc(ball));
+          base = __shfl_sync(act, base, leader);
+          if (take) {
+            const uint32_t wj = j < 2 ? w[0] : j < 4 ? w[1] : j < 6 ? w[2] : w[3];
+            const int slot = base + __popc(ball & ((1u << lane) - 1u));
+            if (slot < kCap) cand[slot] = pack_cand(key_of((wj >> ((j & 1) * 16)) & 0xFFFFu), i0 + j);
+          }
+        }
+      };
+      for_each8(
+          row, n, v,
+          [&](int64_t i0, const uint4 &q) {
+            const unsigned act = __activemask();
+            const unsigned hit = __hge2_mask(as_h2(q.x), b2) | __hge2_mask(as_h2(q.y), b2) |
+                                 __hge2_mask(as_h2(q.z), b2) | __hge2_mask(as_h2(q.w), b2);
+            if (__any_sync(act, hit != 0u)) {
+              const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+              uint32_t pend = 0;
+              if (hit) {
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                  if (key_of((w[j >> 1] >> ((j & 1) * 16)) & 0xFFFFu) >= bound) pend |= 1u << j;
+              }
+              append(act, pend, w, i0);
+            }
+          },
+          [&](int64_t i, uint32_t h) {
+            const uint32_t w[4] = {h, 0u, 0u, 0u};
+            append(__activemask(), key_of(h) >= bound ? 1u : 0u, w, i);
+          });
+      __syncthreads();
+      const int cnt = s_cnt;
+      if (cnt <= kCap) {  // uniform
+        int mc = 1;
+        while (mc < cnt) mc <<= 1;
+        for (int i = cnt + tid; i < mc; i += kThreads) cand[i] = 0ull;
+        __syncthreads();
+        if (mc <= 256) {  // small: warp 0 alone, no block barriers
+          if (tid < 32) sort_desc<true>(cand, mc);
+          __syncthreads();
+        } else {
+          sort_desc<false>(cand, mc);
+        }
+        for (int i = tid; i < k; i += kThreads) {
+          const unsigned long long c = cand[i];
+          const int64_t o = (int64_t)blockIdx.x * k + i;
+          out_idx[o] = (int32_t)(0xFFFFFFFFu - (uint32_t)(c & 0xFFFFFFFFull));
+          out_val[o] = half_bits_of((uint32_t)(c >> 32));
+        }
+        return;
+      }
+    }
+    __syncthreads();
+  }
 
   // ---- radix select of the k-th largest key ----
   uint32_t thr = 0;
@@ -175,7 +346,7 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(int32_t *out_idx, uint16
       if (key > thr) {
         const int slot = atomicAdd(&s_gt, 1);
         if (slot < kMaxK)
-          cand[slot] = ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)(i0 + j));
+          cand[slot] = pack_cand(key, i0 + j);
       }
       ties += (need > 0 && key == thr) ? 1 : 0;
     }
@@ -186,7 +357,7 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(int32_t *out_idx, uint16
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         if (key_of(h[j]) == thr && pos < need) {
-          cand[n_gt + pos] = ((unsigned long long)thr << 32) | (0xFFFFFFFFu - (uint32_t)(i0 + j));
+          cand[n_gt + pos] = pack_cand(thr, i0 + j);
           ++pos;
         }
       }
@@ -202,21 +373,7 @@ __global__ void __launch_bounds__(kThreads) topk_kernel(int32_t *out_idx, uint16
   // ---- bitonic sort, descending, over the next power of two >= k ----
   int m = 1;
   while (m < k) m <<= 1;
-  for (int size = 2; size <= m; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < m / 2; i += kThreads) {
-        const int lo = 2 * i - (i & (stride - 1));
-        const int hi = lo + stride;
-        const bool desc = (lo & size) == 0;
-        const unsigned long long a = cand[lo], b = cand[hi];
-        if ((a < b) == desc) {
-          cand[lo] = b;
-          cand[hi] = a;
-        }
-      }
-      __syncthreads();
-    }
-  }
+  sort_desc<false>(cand, m);
   for (int i = tid; i < k; i += kThreads) {
     const unsigned long long c = cand[i];
     const int64_t o = (int64_t)blockIdx.x * k + i;
