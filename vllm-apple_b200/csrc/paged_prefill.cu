@@ -19,6 +19,8 @@
 //     absolute position.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include <cudaTypedefs.h>
 
@@ -553,6 +555,27 @@ bool encode_page_map(CUtensorMap *m, const void *base, int nhd, int64_t nb, int 
   return r == CUDA_SUCCESS;
 }
 
+// Side stream of the one-token rows: they are HBM-bound split-KV decode work
+// and run beside the compute-bound tile kernel (they fill the SMs the tiles'
+// last wave leaves idle).  Forked from and joined to the caller's stream with
+// events, so stream capture sees an ordinary fork / join.  One set per device;
+// the mutex orders concurrent callers' use of the shared events.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+std::mutex g_side_mu;
+SideStream g_side[64];
+
+bool side_concurrency_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char *e = getenv("VA_PREFILL_CONCURRENT");
+    on = (e && atoi(e) == 0) ? 0 : 1;
+  }
+  return on == 1;
+}
+
 int group_chunk(int g) {
   for (int c = 8; c >= 1; --c)
     if (g % c == 0) return c;
@@ -671,13 +694,42 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
                                         pl.route ? singles_n : nullptr,
                                         use_tc ? order : nullptr, err_flag);
   if (va_host::launch_status() != VA_OK) return VA_ERR_LAUNCH;
-  if (pl.route) {
-    const int rc = va_internal::decode_rows(
+  auto launch_rows = [&](cudaStream_t rs) {
+    return va_internal::decode_rows(
         out, q, k_cache, v_cache, block_table, singles, singles_n, token_to_seq, positions,
         pl.rows_bound,
         num_seqs, num_query_heads, num_kv_heads, head_size, block_size, max_blocks_per_seq,
         num_blocks, scale, s_block, s_head, s_token, q_s_token, q_s_head, o_s_token, o_s_head,
-        ws + pl.o_dec, pl.dec_bytes, err_flag, st);
+        ws + pl.o_dec, pl.dec_bytes, err_flag, rs);
+  };
+  // the rows go beside the tile kernel on the side stream when the tiles run on
+  // the tensor-core kernel; otherwise (and if the side stream cannot be set up)
+  // in order on the caller's stream
+  SideStream *side = nullptr;
+  std::unique_lock<std::mutex> side_lock(g_side_mu, std::defer_lock);
+  if (pl.route && use_tc && side_concurrency_enabled()) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64) {
+      side_lock.lock();
+      SideStream &ss = g_side[dev];
+      cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+      cudaStreamIsCapturing(st, &cap);
+      // created outside stream capture only (the first eager call does it)
+      if (!ss.s && cap == cudaStreamCaptureStatusNone) {
+        if (cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) != cudaSuccess) {
+          cudaGetLastError();
+          ss = SideStream{};
+        }
+      }
+      if (ss.s) side = &ss;
+      else side_lock.unlock();
+    }
+  }
+  if (pl.route && !side) {
+    const int rc = launch_rows(st);
     if (rc != VA_OK) return rc;
   }
 
@@ -727,8 +779,18 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
     const int64_t nblk = mt * (int64_t)grid.y;
     if (nblk > INT32_MAX) return VA_ERR_UNSUPPORTED;
     const dim3 grid1((unsigned)nblk);
-    return head_size == 64 ? launch_tc_g<64>(gc, t, mk, mv, grid1, st)
-                           : launch_tc_g<128>(gc, t, mk, mv, grid1, st);
+    if (side && cudaEventRecord(side->fork, st) != cudaSuccess) return VA_ERR_LAUNCH;
+    const int rc = head_size == 64 ? launch_tc_g<64>(gc, t, mk, mv, grid1, st)
+                                   : launch_tc_g<128>(gc, t, mk, mv, grid1, st);
+    if (!side) return rc;
+    // join even when the tile launch failed, so the caller's stream never
+    // runs ahead of the rows
+    if (cudaStreamWaitEvent(side->s, side->fork, 0) != cudaSuccess) return VA_ERR_LAUNCH;
+    const int rr = launch_rows(side->s);
+    if (cudaEventRecord(side->join, side->s) != cudaSuccess ||
+        cudaStreamWaitEvent(st, side->join, 0) != cudaSuccess)
+      return VA_ERR_LAUNCH;
+    return rc != VA_OK ? rc : rr;
   }
   switch (head_size) {
     case 32: return launch_g<32>(gc, a, grid, st);
