@@ -51,49 +51,65 @@ VA_DEVINL float block_sum(float v, float *red) {
   return t;
 }
 
+// Rows are processed grid-stride; the next row's loads are issued before the
+// current row is reduced, normalised and stored, so every CTA keeps a row in
+// flight from HBM while it works on the previous one.
 template <int VPT, bool RES>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(
-    __half *out, const __half *x, const __half *w, const __half *res, int64_t hidden, float eps,
-    int64_t xs, int64_t os, int64_t rs) {
-  __shared__ float red[kNormThreads / 32];
-  const int64_t row = blockIdx.x;
+    __half *out, const __half *x, const __half *w, const __half *res, int64_t T, int64_t hidden,
+    float eps, int64_t xs, int64_t os, int64_t rs) {
+  __shared__ float red[2][kNormThreads / 32];  // alternating rows: one barrier per row
   const int nvec = (int)(hidden / 8);
-  const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * xs);
-  uint4 v[VPT];
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int c = threadIdx.x + i * kNormThreads;
-    if (c < nvec) {
-      v[i] = va::ldg_stream(xr + c);
-      float f[8];
-      unpack8(v[i], f);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss = __fadd_rn(ss, __fmul_rn(f[j], f[j]));
-    }
-  }
-  const float tot = block_sum<kNormThreads>(ss, red);
-  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)hidden), eps)));
   const uint4 *wr = reinterpret_cast<const uint4 *>(w);
-  uint4 *orow = reinterpret_cast<uint4 *>(out + row * os);
+  auto load = [&](int64_t row, uint4 (&v)[VPT]) {
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * xs);
 #pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int c = threadIdx.x + i * kNormThreads;
-    if (c < nvec) {
-      float f[8], g[8];
-      unpack8(v[i], f);
-      unpack8(__ldg(wr + c), g);
-      float y[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) y[j] = __fmul_rn(__fmul_rn(f[j], r), g[j]);
-      if (RES) {
-        float q[8];
-        unpack8(va::ldg_stream(reinterpret_cast<const uint4 *>(res + row * rs) + c), q);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) y[j] = __fadd_rn(y[j], q[j]);
-      }
-      orow[c] = pack8(y);
+    for (int i = 0; i < VPT; ++i) {
+      const int c = threadIdx.x + i * kNormThreads;
+      if (c < nvec) v[i] = va::ldg_stream(xr + c);
     }
+  };
+  uint4 cur[VPT], nxt[VPT];
+  int64_t row = blockIdx.x;
+  if (row < T) load(row, cur);
+  for (int it = 0; row < T; row += gridDim.x, ++it) {
+    const int64_t next = row + gridDim.x;
+    if (next < T) load(next, nxt);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = threadIdx.x + i * kNormThreads;
+      if (c < nvec) {
+        float f[8];
+        unpack8(cur[i], f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = __fadd_rn(ss, __fmul_rn(f[j], f[j]));
+      }
+    }
+    const float tot = block_sum<kNormThreads>(ss, red[it & 1]);
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)hidden), eps)));
+    uint4 *orow = reinterpret_cast<uint4 *>(out + row * os);
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int c = threadIdx.x + i * kNormThreads;
+      if (c < nvec) {
+        float f[8], g[8];
+        unpack8(cur[i], f);
+        unpack8(__ldg(wr + c), g);
+        float y[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] = __fmul_rn(__fmul_rn(f[j], r), g[j]);
+        if (RES) {
+          float q[8];
+          unpack8(va::ldg_stream(reinterpret_cast<const uint4 *>(res + row * rs) + c), q);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) y[j] = __fadd_rn(y[j], q[j]);
+        }
+        orow[c] = pack8(y);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) cur[i] = nxt[i];
   }
 }
 
@@ -120,14 +136,30 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_any_kernel(
   }
 }
 
+// Grid: as many CTAs as fit on the GPU at once (rows are walked grid-stride).
+template <int VPT, bool RES>
+unsigned norm_grid(int64_t T) {
+  static int per_sm = 0;
+  if (!per_sm) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rmsnorm_vec_kernel<VPT, RES>,
+                                                      kNormThreads, 0) != cudaSuccess ||
+        per_sm < 1)
+      per_sm = 1;
+  }
+  const int64_t cap = (int64_t)va_host::sm_count() * per_sm;
+  return (unsigned)(T < cap ? T : cap);
+}
+
 template <int VPT>
-void launch_norm_vec(bool r, dim3 g, cudaStream_t st, __half *o, const __half *x,
+void launch_norm_vec(bool r, int64_t T, cudaStream_t st, __half *o, const __half *x,
                      const __half *w, const __half *res, int64_t h, float eps, int64_t xs,
                      int64_t os, int64_t rs) {
   if (r)
-    rmsnorm_vec_kernel<VPT, true><<<g, kNormThreads, 0, st>>>(o, x, w, res, h, eps, xs, os, rs);
+    rmsnorm_vec_kernel<VPT, true><<<norm_grid<VPT, true>(T), kNormThreads, 0, st>>>(
+        o, x, w, res, T, h, eps, xs, os, rs);
   else
-    rmsnorm_vec_kernel<VPT, false><<<g, kNormThreads, 0, st>>>(o, x, w, res, h, eps, xs, os, rs);
+    rmsnorm_vec_kernel<VPT, false><<<norm_grid<VPT, false>(T), kNormThreads, 0, st>>>(
+        o, x, w, res, T, h, eps, xs, os, rs);
 }
 
 // ---------------------------------------------------------------------------
@@ -306,14 +338,14 @@ extern "C" int va_rmsnorm(void *out, const void *x, const void *weight, const vo
   const int64_t vpt = (hidden_size / 8 + kNormThreads - 1) / kNormThreads;
   if (vec && vpt <= 8) {
     switch (vpt) {
-      case 1: launch_norm_vec<1>(res, g, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
-      case 2: launch_norm_vec<2>(res, g, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
-      case 3: launch_norm_vec<3>(res, g, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
-      case 4: launch_norm_vec<4>(res, g, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
-      case 5: launch_norm_vec<5>(res, g, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
-      case 6: launch_norm_vec<6>(res, g, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
-      case 7: launch_norm_vec<7>(res, g, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
-      default: launch_norm_vec<8>(res, g, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
+      case 1: launch_norm_vec<1>(res, num_tokens, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
+      case 2: launch_norm_vec<2>(res, num_tokens, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
+      case 3: launch_norm_vec<3>(res, num_tokens, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
+      case 4: launch_norm_vec<4>(res, num_tokens, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
+      case 5: launch_norm_vec<5>(res, num_tokens, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
+      case 6: launch_norm_vec<6>(res, num_tokens, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
+      case 7: launch_norm_vec<7>(res, num_tokens, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
+      default: launch_norm_vec<8>(res, num_tokens, st, o, xi, w, r, hidden_size, eps, x_s_token, out_s_token, res_s_token); break;
     }
   } else if (res) {
     rmsnorm_any_kernel<true><<<g, kNormThreads, 0, st>>>(o, xi, w, r, hidden_size, eps, x_s_token,
