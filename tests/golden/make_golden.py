@@ -1,7 +1,7 @@
 """Generate the golden fixtures of this directory by running the REFERENCE.
 
-Run in a container where the reference tree is mounted (default
-/root/reference, override with VA_REFERENCE_ROOT); the outputs are committed
+Run in a container where the reference tree is mounted (its location is
+VA_REFERENCE_ROOT, with the mount point as the default); the outputs are committed
 and the tests read only them, so nothing at test time needs the reference.
 
 What runs (all reference code, unmodified):
