@@ -93,3 +93,47 @@ def test_prefill_skips_invalid_tokens():
     assert torch.all(out[1].cpu() == 7.0) and torch.all(out[5].cpu() == 7.0)
     keep = [i for i in range(c.num_tokens) if i not in (1, 5)]
     assert max_abs(np16(out)[keep], o[keep]) <= ATOL
+
+
+@pytest.mark.parametrize("bs", [8, 32, 64])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("layout", ["hnd", "nhd"])
+def test_prefill_block_sizes(bs, D, layout):
+    """Pages of 8..64 tokens: chunk-to-page arithmetic, TMA boxes per lane, the
+    row-by-row copy of the page holding the end of the context."""
+    from vllm_apple_b200.workloads import make_mixed_case
+    c = make_mixed_case(D=D, bs=bs, layout=layout, num_chunks=3, chunk=150, prior=(0, 700),
+                        num_decode=4, decode_len=(1, 500), seed=bs + D)
+    out, _, _, bad = _run(c)
+    assert bad == 0
+    o, _, _ = _oracle(c)
+    assert max_abs(np16(out), o) <= ATOL
+
+
+def test_prefill_bad_block_is_flagged_and_skipped():
+    """An out-of-range block id inside a chunk's context: tokens that would read it
+    are left unwritten and the bad-block flag is raised; earlier tokens are exact."""
+    from vllm_apple_b200 import ops
+    from vllm_apple_b200.workloads import make_mixed_case
+    c = make_mixed_case(num_chunks=1, chunk=200, prior=(300, 300), num_decode=0, seed=9)
+    bs = c.bs
+    page = (300 + 100) // bs           # a page covering chunk positions ~400
+    bt = c.block_table.clone()
+    bt[0, page] = c.num_blocks + 7
+    ops = _ops()
+    dk, dv = c.k_cache.cuda(), c.v_cache.cuda()
+    ops.kv_write_slots(dk, dv, c.k.cuda(), c.v.cuda(), c.slot_mapping.cuda(), c.layout)
+    q = c.q.cuda()
+    out = torch.full_like(q, 7.0)
+    ops.paged_prefill(out, q, dk, dv, bt.cuda(), c.token_to_seq.cuda(), c.positions.cuda(),
+                      scale=c.scale, layout=c.layout)
+    torch.cuda.synchronize()
+    flags = ops.check_device_errors(raise_on_error=False)
+    assert flags & 2  # VA_FLAG_BAD_BLOCK
+    o, _, _ = _oracle(c)
+    pos = c.positions.numpy()
+    first_bad = page * bs
+    good = pos < first_bad
+    assert good.any() and (~good).any()
+    assert max_abs(np16(out)[good], o[good]) <= ATOL
+    assert torch.all(out.cpu()[torch.from_numpy(~good)] == 7.0)
