@@ -183,8 +183,15 @@ struct Cfg {
                 "merge buffers must fit in the stage area");
 };
 
+// Small heads with a large GQA group (D <= 64, GC >= 5: the Qwen shape) do ~3x the
+// arithmetic per KV byte of the 22B shape; their register demand (q of every head
+// in registers) would cap them at 3 CTAs per SM, so they are held to 4.
+template <int D, int GC>
+constexpr int decode_min_blocks() { return (D <= 64 && GC >= 5) ? 4 : 1; }
+
 template <int D, int GC, int BS>
-__global__ void __launch_bounds__(kNW * 32) paged_decode_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(kNW * 32, decode_min_blocks<D, GC>())
+    paged_decode_kernel(const DecodeArgs a) {
   using C = Cfg<D, GC, BS>;
   constexpr int GP = C::GP, TPT = C::TPT, TOK = C::TOK, DPL = C::DPL, DV = C::DV;
   constexpr int NPASS = C::NPASS, R = C::R, PAGE = C::PAGE;
