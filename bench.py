@@ -422,6 +422,198 @@ def run_reference(args, world, rank):
     }
 
 
+# ---------------------------------------------------------------------------
+# the other hot-path rows (one GPU): --row mixed | rmsnorm | rope | silu_mul | topk
+# ---------------------------------------------------------------------------
+ROWS = ("decode", "mixed", "rmsnorm", "rope", "silu_mul", "topk")
+
+
+def tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured (cuBLAS bf16 burst)"
+    return 1590.0, "fallback"
+
+
+def time_each(fn, steps, warmup, flush):
+    """Device time (ms) of `steps` calls of fn: CUDA events around each call on the
+    current stream, L2 flushed (a write larger than L2) between calls."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    for s, e in evs:
+        flush.zero_()
+        s.record()
+        fn()
+        e.record()
+    torch.cuda.synchronize()
+    return sum(s.elapsed_time(e) for s, e in evs)
+
+
+def cpu_time(fn, budget_s):
+    fn()
+    times, t_end = [], time.perf_counter() + budget_s
+    while True:
+        t = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t)
+        if time.perf_counter() > t_end or len(times) >= 5:
+            return min(times), len(times)
+
+
+def row_case(row, dev):
+    """(step fn, algorithmic bytes, flops or None, launches per step, config, cpu leg)
+    of one row at its BASELINE shape; the cpu leg times the oracle restatement of the
+    reference on a bounded sample and returns (value, unit, sample text)."""
+    from vllm_apple_b200 import ops
+    from vllm_apple_b200.workloads import make_elementwise_case, make_mixed_case
+    from oracle import paged_attention as ref
+    if row == "mixed":
+        m = make_mixed_case(device=dev, seed=0)
+        q, k, v = m.q.to(dev), m.k.to(dev), m.v.to(dev)
+        bt, ts, ps, sm = (m.block_table.to(dev), m.token_to_seq.to(dev), m.positions.to(dev),
+                          m.slot_mapping.to(dev))
+        out = torch.empty_like(q)
+
+        def step():
+            ops.kv_write_slots(m.k_cache, m.v_cache, k, v, sm)
+            ops.paged_prefill(out, q, m.k_cache, m.v_cache, bt, ts, ps, scale=m.scale)
+
+        pos = m.positions.long()
+        flops = 4 * m.Hq * m.D * int((pos + 1).sum())
+        ctx = [int(pos[m.token_to_seq.long() == s].max()) + 1 for s in range(len(m.seq_lens))]
+        nbytes = (sum(ctx) * m.Hkv * m.D * 4 + m.num_tokens * (m.Hq + 2 * m.Hkv) * m.D * 2
+                  + m.num_tokens * m.Hq * m.D * 2 + m.num_tokens * m.Hkv * m.D * 4)
+        cfg = {"workload": "mixed_22b", "tokens": m.num_tokens, "prefill_chunks": "4 x 512",
+               "prior": "U[0,4096]", "decode_rows": m.num_decode_tokens, "Hq": m.Hq,
+               "Hkv": m.Hkv, "head_size": m.D, "block_size": m.bs}
+
+        def cpu(budget):
+            c = make_mixed_case(device="cpu", seed=0, num_chunks=1, chunk=64, prior=(0, 512),
+                                num_decode=4, decode_len=(256, 1024))
+            kc, vc = c.k_cache.numpy().copy(), c.v_cache.numpy().copy()
+
+            def one():
+                ref.kv_write_slots_vectorized(kc, vc, c.k.numpy(), c.v.numpy(),
+                                              c.slot_mapping.numpy(), c.layout)
+                ref.paged_prefill(c.q.numpy(), kc, vc, c.block_table.numpy(),
+                                  c.token_to_seq.numpy(), c.positions.numpy(), c.scale,
+                                  layout=c.layout)
+            sec, n = cpu_time(one, budget)
+            f = 4 * c.Hq * c.D * int((c.positions.long() + 1).sum())
+            return f / sec / 1e12, "TFLOP/s", (f"1 chunk of 64 tokens over <=512 prior + 4 decode "
+                                               f"rows (numpy float64), best of {n}")
+        return step, nbytes, flops, 5, cfg, cpu
+    e = make_elementwise_case(device=dev, seed=0)
+    T, H = e.x.shape
+    if row == "rmsnorm":
+        out = torch.empty_like(e.x)
+        step = lambda: ops.rmsnorm(out, e.x, e.w, e.eps)  # noqa: E731
+        nbytes = 2 * T * H * 2 + H * 2
+        cfg = {"workload": "rmsnorm_8192x5120", "eps": e.eps}
+
+        def cpu(budget):
+            n = 512
+            x, w = e.x[:n].cpu().numpy(), e.w.cpu().numpy()
+            sec, k = cpu_time(lambda: ref.rmsnorm(x, w, e.eps), budget)
+            return 2 * n * H * 2 / sec / 1e9, "GB/s", f"first {n} tokens (numpy), best of {k}"
+        return step, nbytes, None, 1, cfg, cpu
+    if row == "rope":
+        c, sn = ref.rope_cos_sin_cache(e.q.shape[2], e.max_position, e.theta)
+        cd, sd = torch.from_numpy(c).to(dev), torch.from_numpy(sn).to(dev)
+        step = lambda: ops.rope(e.q, e.k, cd, sd, e.positions)  # noqa: E731
+        nel = T * (e.q.shape[1] + e.k.shape[1]) * e.q.shape[2]
+        nbytes = 2 * nel * 2 + T * 4
+        cfg = {"workload": "rope_neox_8192", "theta": e.theta, "Hq": e.q.shape[1],
+               "Hkv": e.k.shape[1], "head_size": e.q.shape[2],
+               "note": "cos/sin table (L2-resident) excluded from bytes"}
+
+        def cpu(budget):
+            n = 256
+            q, k, p = e.q[:n].cpu().numpy(), e.k[:n].cpu().numpy(), e.positions[:n].cpu().numpy()
+            sec, m = cpu_time(lambda: ref.rope(q, k, c, sn, p), budget)
+            b = 2 * n * (e.q.shape[1] + e.k.shape[1]) * e.q.shape[2] * 2
+            return b / sec / 1e9, "GB/s", f"first {n} tokens (numpy), best of {m}"
+        return step, nbytes, None, 1, cfg, cpu
+    if row == "silu_mul":
+        out = torch.empty_like(e.gate)
+        step = lambda: ops.silu_mul(out, e.gate, e.up)  # noqa: E731
+        nbytes = 3 * e.gate.numel() * 2
+        cfg = {"workload": "silu_mul_8192x32768"}
+
+        def cpu(budget):
+            n = 64
+            g, u = e.gate[:n].cpu().numpy(), e.up[:n].cpu().numpy()
+            sec, m = cpu_time(lambda: ref.silu_mul(g, u), budget)
+            return 3 * g.size * 2 / sec / 1e9, "GB/s", f"first {n} tokens (numpy), best of {m}"
+        return step, nbytes, None, 1, cfg, cpu
+    if row == "topk":
+        g = torch.Generator().manual_seed(0)
+        Tk, V, k = 1024, 131072, 50
+        x = (torch.randn(Tk, V, generator=g) * 3).half()
+        xd = x.to(dev)
+        idx = torch.empty(Tk, k, dtype=torch.int32, device=dev)
+        val = torch.empty(Tk, k, dtype=torch.float16, device=dev)
+        step = lambda: ops.topk(idx, val, xd, k)  # noqa: E731
+        nbytes = Tk * V * 2 + Tk * k * 6
+        cfg = {"workload": "topk_1024x131072", "k": k}
+
+        def cpu(budget):
+            n = 8
+            xs = x[:n].numpy()
+            sec, m = cpu_time(lambda: ref.topk(xs, k), budget)
+            return (n * V * 2 + n * k * 6) / sec / 1e9, "GB/s", f"first {n} rows (numpy), best of {m}"
+        return step, nbytes, None, 1, cfg, cpu
+    raise ValueError(row)
+
+
+def run_row(args, rank, local):
+    if rank != 0:
+        return None
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    from vllm_apple_b200 import ops
+    step, nbytes, flops, launches, cfg, cpu = row_case(args.row, dev)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MB > L2
+    with ClockSampler(local) as clk:
+        ms = time_each(step, args.steps, args.warmup, flush)
+    ops.check_device_errors(local)
+    ms_step = ms / args.steps
+    gbs = nbytes / (ms_step * 1e-3) / 1e9
+    hbm, hbm_kind = peaks()
+    if flops is not None:
+        tf = flops / (ms_step * 1e-3) / 1e12
+        tpk, tkind = tensor_peak()
+        metric, value, unit = "mixed-batch step TFLOP/s (causal prefill FLOPs)", tf, "TFLOP/s"
+        roof = {"bound": "tensor", "achieved": round(tf, 2), "peak": tpk, "unit": "TFLOP/s",
+                "frac": round(tf / tpk, 4), "peak_kind": tkind, "traffic": None,
+                "note": "whole step (KV scatter, planner, tiles and decode rows); the decode "
+                        "rows are HBM-bound: GB/s below"}
+    else:
+        metric, value, unit = f"{args.row} HBM GB/s (algorithmic bytes)", gbs, "GB/s"
+        roof = {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(gbs / hbm, 4), "peak_kind": hbm_kind, "traffic": None,
+                "algorithmic_bytes_per_launch": int(nbytes)}
+    res = {"metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": 1,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+           "data": "synthetic (seeded N(0,1) fp16, BASELINE shapes)",
+           "config": dict(cfg, l2="flushed between timed calls (256 MB write)"),
+           "GBps": round(gbs, 1), "roofline": roof, "gpu_launches": args.steps * launches,
+           "clocks": clk.summary()}
+    if args.cpu_budget > 0:
+        threads = os.cpu_count() or 1
+        torch.set_num_threads(threads)
+        v, u, sample = cpu(args.cpu_budget)
+        res["cpu_baseline"] = {"value": round(v, 4), "unit": u, "cores": 1, "kind": "port",
+                               "sample": sample + "; oracle restatement of the reference's "
+                                         "CPU formula"}
+    return res
+
+
 def main():
     global WORKLOAD
     ap = argparse.ArgumentParser()
@@ -434,6 +626,8 @@ def main():
     ap.add_argument("--workload", default=WORKLOAD,
                     help="decode config of vllm_apple_b200.workloads (default: %(default)s)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end leg")
+    ap.add_argument("--row", choices=ROWS, default="decode",
+                    help="hot-path row to measure (default: the headline decode step)")
     args = ap.parse_args()
     WORKLOAD = args.workload
     if args.warmup < 3:
@@ -441,6 +635,8 @@ def main():
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":
         res = run_reference(args, world, rank)
+    elif args.row != "decode":
+        res = run_row(args, rank, local)
     else:
         res = run_ours(args, world, rank, local)
     if res is not None:
