@@ -499,12 +499,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int j = 0; j < nch; ++j) {
         if (j < nj) issue_pv(j);
+        // stage j is free once PV(j) (and S(j), issued earlier) completes: release it
+        // before S(j+2) goes in, so the producer's refill is not held behind it
+        if (lane == 0 && !dead()) umma_commit(&bar_empty[j % kStages]);
+        __syncwarp();
         if (j + 2 < nch) {
           wait_chunk(j + 2);
           if (j + 2 < nj) issue_s(j + 2);
         }
-        if (lane == 0 && !dead()) umma_commit(&bar_empty[j % kStages]);
-        __syncwarp();
       }
       // teardown: every MMA issued by this thread has retired
       if (lane == 0) {
