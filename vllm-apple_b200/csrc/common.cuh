@@ -30,6 +30,11 @@ VA_DEVINL void mbar_init(uint64_t *bar, uint32_t count) {
                : "memory");
 }
 
+// Invalidate a barrier whose phases have all completed (before re-initialising it).
+VA_DEVINL void mbar_inval(uint64_t *bar) {
+  asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 // Make barrier initialisation visible to the async (bulk-copy) proxy.
 VA_DEVINL void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");

@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(1024) plan_tiles_kernel(const int32_t *token_t
   if (tid == 0) {
     *tiles_n = n;
     if (singles_n) *singles_n = n_single;
+    tiles_n[2] = 0;  // item counter of the persistent tile kernel
   }
   if (!order) return;
   // bucket b holds tiles whose last token sees about 64 * (kOrderBuckets - 1 - b) keys
@@ -763,6 +764,7 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
     tc::Args t{};
     t.out = a.out; t.q = a.q; t.kc = a.kc; t.vc = a.vc; t.bt = a.bt; t.tok_seq = a.tok_seq;
     t.pos = a.pos; t.tiles = a.tiles; t.order = order; t.tiles_n = a.tiles_n; t.err = a.err;
+    t.work = tiles_n + 2;
     t.num_seqs = a.num_seqs; t.max_blocks = a.max_blocks; t.num_blocks = a.num_blocks;
     t.Hq = a.Hq; t.Hkv = a.Hkv; t.G = a.G; t.hgroups = a.hgroups; t.TQ = a.TQ / tc::kTiles;
     t.bs = a.bs;
@@ -775,10 +777,12 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
     if (!encode_page_map(&mk, k_cache, layout, num_blocks, num_kv_heads, block_size, head_size) ||
         !encode_page_map(&mv, v_cache, layout, num_blocks, num_kv_heads, block_size, head_size))
       return VA_ERR_LAUNCH;
-    // one dimension, tile-major: blocks launch in the planner's longest-first order
-    const int64_t nblk = mt * (int64_t)grid.y;
-    if (nblk > INT32_MAX) return VA_ERR_UNSUPPORTED;
-    const dim3 grid1((unsigned)nblk);
+    // persistent: one CTA per SM (shared memory and TMEM allow no more), items
+    // taken in the planner's longest-first order
+    const int64_t nitems = mt * (int64_t)grid.y;
+    if (nitems > INT32_MAX) return VA_ERR_UNSUPPORTED;
+    const int64_t nsm = va_host::sm_count();
+    const dim3 grid1((unsigned)(nitems < nsm ? nitems : nsm));
     if (side && cudaEventRecord(side->fork, st) != cudaSuccess) return VA_ERR_LAUNCH;
     const int rc = head_size == 64 ? launch_tc_g<64>(gc, t, mk, mv, grid1, st)
                                    : launch_tc_g<128>(gc, t, mk, mv, grid1, st);

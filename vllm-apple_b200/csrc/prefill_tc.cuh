@@ -217,6 +217,7 @@ struct Args {
   const int2 *tiles;
   const int32_t *order;  // tile indices, longest context first
   const int32_t *tiles_n;
+  int32_t *work;  // item counter (zeroed by the planner)
   int32_t *err;
   int64_t num_seqs, max_blocks, num_blocks;
   int Hq, Hkv, G, hgroups;
@@ -260,66 +261,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *bar_done = bar_pv + kTiles;      // [kTiles] every MMA of the tile retired
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_done + kTiles);
   int *s_pos = reinterpret_cast<int *>(smem + S::oPos);  // [kTiles][kRows]
-  __shared__ int s_ctx[kTiles], s_bad_from, s_dead;
+  __shared__ int s_ctx[kTiles], s_bad_from, s_dead, s_item[2];
 
   const int ny = a.Hkv * a.hgroups;
-  const int item = (int)(blockIdx.x / (unsigned)ny);
-  if (item >= *a.tiles_n) return;
-  const int tile = a.order[item];
-  const int2 td = a.tiles[tile];
-  const int t0 = td.x, nq = td.y;
-  if (nq == 1 && a.skip_singles) return;  // handled by the split-KV decode kernel
-  const int seq = a.tok_seq[t0];
-  const int yb = (int)(blockIdx.x - (unsigned)item * ny);
-  const int kvh = yb / a.hgroups;
-  const int hg = yb - kvh * a.hgroups;
-  const int head0 = kvh * a.G + hg * GC;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int BS = a.bs, TQ = a.TQ;
-
-  if (tid < kTiles) s_ctx[tid] = 0;
-  if (tid == 0) { s_bad_from = INT_MAX; s_dead = 0; }
-  __syncthreads();
-  if (tid < kSoftmax) {
-    const int h = tid / kRows, tk = tid % kRows;
-    int p = -1;
-    const int ti = h * TQ + tk;
-    if (tk < TQ && ti < nq && seq >= 0 && seq < a.num_seqs) {
-      p = a.pos[t0 + ti];
-      if (p >= 0 && (int64_t)((p + BS) / BS) > a.max_blocks) {
-        va::raise_flag(a.err, VA_FLAG_CTX_OVERFLOW);
-        p = -1;
-      }
-      if (p < 0) p = -1;
-    }
-    s_pos[tid] = p;
-    if (p >= 0) atomicMax(&s_ctx[h], p + 1);
-  }
-  if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      va::mbar_init(&bar_full[i], 1);
-      va::mbar_init(&bar_empty[i], kTiles);
-    }
-    for (int i = 0; i < 2 * kTiles; ++i) va::mbar_init(&bar_s[i], 1);
-    for (int i = 0; i < kTiles; ++i) {
-      va::mbar_init(&bar_p[i], kRows);
-      va::mbar_init(&bar_pv[i], 1);
-      va::mbar_init(&bar_done[i], 1);
-    }
-    va::fence_barrier_init();
-  }
+  const int nitems = *a.tiles_n * ny;
+  if ((int)blockIdx.x >= nitems) return;
+  if (tid == 0) s_dead = 0;
   if (warp == kMmaWarp) tmem_alloc(tmem_slot, kTmemCols);
   fence_before_sync();
   __syncthreads();
   fence_after_sync();
-  const int ctx = max(s_ctx[0], s_ctx[1]);
   const uint32_t tmem = *tmem_slot;
-  if (ctx == 0) {  // nothing to attend (all tokens skipped): release TMEM and leave
-    if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
-    return;
-  }
-  const int nch = (ctx + kKeys - 1) / kKeys;
-  const int32_t *bt_row = a.bt + (int64_t)seq * a.max_blocks;
   constexpr int CPR = D / 8;  // 16-byte pieces per row
 
   auto dead = [&]() { return *(volatile int *)&s_dead != 0; };
@@ -330,337 +284,406 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (dead()) return;
     if (!va::mbar_wait_bounded(bar, parity, kWaitLimit)) timeout();
   };
+  bool inited = false;  // thread 0: the mbarriers hold an earlier item's state
 
-  if (warp == kProducerWarp) {
-    // =================== producer: K/V chunks into the stages ===================
-    const int npc = kKeys / BS;  // a power of two <= 8: a chunk never straddles a group
-    const int pages = (ctx + BS - 1) / BS;  // <= max_blocks (checked above)
-    const int tail_rows = ctx - (pages - 1) * BS;  // rows of the last page inside the context
-    // block ids are read 32 pages (one per lane) at a time, one group ahead
-    auto load_group = [&](int g) -> int32_t {
-      const int page = g * 32 + lane;
-      return page < pages ? __ldg(bt_row + page) : -1;
-    };
-    int gi = 0;
-    int32_t g_cur = load_group(0), g_next = load_group(1);
+  // Persistent: each CTA takes (tile pair, kv head) items from a counter in the
+  // planner's order (longest context first) until none is left.
 #pragma unroll 1
-    for (int c = 0; c < nch; ++c) {
-      const int buf = c % kStages;
-      const int first = c * npc;
-      if ((first >> 5) != gi) {
-        gi = first >> 5;
-        g_cur = g_next;
-        g_next = load_group(gi + 1);
-      }
-      const int32_t gid = __shfl_sync(0xffffffffu, g_cur, (first & 31) + (lane & (npc - 1)));
-      if (c >= kStages) wait_bar(&bar_empty[buf], (uint32_t)(((c / kStages) - 1) & 1));
-      // page ids of this chunk (lane p holds page p)
-      int32_t id = -1;
-      const int page = first + lane;
-      if (lane < npc && page < pages) {
-        id = gid;
-        if (id < 0 || id >= a.num_blocks) {
-          atomicMin(&s_bad_from, page * BS);
-          id = -2;
-        }
-      }
-      unsigned char *kb = smem + S::oK + buf * S::kKV, *vb = smem + S::oV + buf * S::kKV;
-      // by TMA: valid whole pages; by the warp: the partial last page (copied, tail
-      // zeroed) and invalid / past-context pages (zeroed)
-      const bool part = page == pages - 1 && tail_rows < BS;
-      const unsigned valid = __ballot_sync(0xffffffffu, lane < npc && id >= 0 && !part);
-      const unsigned partial = __ballot_sync(0xffffffffu, lane < npc && id >= 0 && part);
-      if (valid != (1u << npc) - 1u) {  // only near the end of the context
-        const int ppage = partial ? __ffs(partial) - 1 : -1;
-        const int32_t pid = __shfl_sync(0xffffffffu, id, ppage < 0 ? 0 : ppage);
-        for (int i = lane; i < kKeys * CPR; i += 32) {
-          const int r = i / CPR, ch16 = i - r * CPR;
-          const int p = r / BS;
-          if ((valid >> p) & 1u) continue;
-          const uint32_t o = sw128_off(r, ch16 * 8, kKeys);
-          uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-          if (p == ppage && r - p * BS < tail_rows) {
-            const int64_t off = (int64_t)pid * a.s_block + (int64_t)kvh * a.s_head +
-                                (int64_t)(r - p * BS) * a.s_token + ch16 * 8;
-            kv = __ldg(reinterpret_cast<const uint4 *>(a.kc + off));
-            vv = __ldg(reinterpret_cast<const uint4 *>(a.vc + off));
-          }
-          *reinterpret_cast<uint4 *>(kb + o) = kv;
-          *reinterpret_cast<uint4 *>(vb + o) = vv;
-        }
-        va::fence_proxy_async_smem();
-        __syncwarp();
-      }
-      if (lane == 0) va::mbar_arrive_expect_tx(&bar_full[buf], __popc(valid) * (2u * BS * D * 2u));
-      __syncwarp();
-      {  // one box per lane: lane = (page, 64-column block, K or V)
-        constexpr int kBoxes = D / 64 * 2;
-        const int p = lane / kBoxes, rem = lane - p * kBoxes;
-        const int kbk = rem >> 1;
-        const int pidl = __shfl_sync(0xffffffffu, id, p & 31);
-        if (p < npc && ((valid >> p) & 1u)) {
-          const uint32_t off = kbk * kKeys * 128 + p * BS * 128;
-          const int c1 = a.nhd ? kvh : 0;
-          const int c2 = a.nhd ? pidl * BS : pidl * a.Hkv + kvh;
-          if (rem & 1)
-            tma_load_3d(vb + off, &tmv, kbk * 64, c1, c2, &bar_full[buf]);
-          else
-            tma_load_3d(kb + off, &tmk, kbk * 64, c1, c2, &bar_full[buf]);
-        }
-      }
-      __syncwarp();
-      if (dead()) break;
-    }
-    // no copy may still be landing when the CTA exits (normally none is: the
-    // MMA warps consumed every chunk); bounded, reports like any other wait
-    if (lane == 0) {
-      for (int c = nch - kStages < 0 ? 0 : nch - kStages; c < nch; ++c)
-        if (!va::mbar_wait_bounded(&bar_full[c % kStages], (uint32_t)((c / kStages) & 1),
-                                   kWaitLimit))
-          timeout();
-    }
-    __syncwarp();
-    all_sync();
-  } else {
-    // ---- Q of both tiles: cp.async by the softmax and MMA warps ----
-    const int mtid = warp > kProducerWarp ? tid - 32 : tid;  // 0 .. kMath - 1
-    for (int i = mtid; i < kTiles * kRows * CPR; i += kMath) {
-      const int r2 = i / CPR, c = i - r2 * CPR;
-      const int h = r2 / kRows, r = r2 - h * kRows;
-      const int tk = r / GC, g = r - tk * GC;
+  for (int iter = 0;; ++iter) {
+    if (tid == 0) s_item[iter & 1] = atomicAdd(a.work, 1);
+    __syncthreads();
+    const int it = s_item[iter & 1];
+    if (it >= nitems || dead()) break;  // uniform
+    const int item = it / ny, yb = it - item * ny;
+    const int tile = a.order[item];
+    const int2 td = a.tiles[tile];
+    const int t0 = td.x, nq = td.y;
+    if (nq == 1 && a.skip_singles) continue;  // handled by the split-KV decode kernel
+    const int seq = a.tok_seq[t0];
+    const int kvh = yb / a.hgroups;
+    const int hg = yb - kvh * a.hgroups;
+    const int head0 = kvh * a.G + hg * GC;
+
+    if (tid < kTiles) s_ctx[tid] = 0;
+    if (tid == 0) s_bad_from = INT_MAX;
+    __syncthreads();
+    if (tid < kSoftmax) {
+      const int h = tid / kRows, tk = tid % kRows;
+      int p = -1;
       const int ti = h * TQ + tk;
-      unsigned char *dst = smem + S::oQ + h * S::kQ + sw128_off(r, c * 8, kRows);
-      if (tk < TQ && ti < nq)
-        cp_async16(dst, a.q + (int64_t)(t0 + ti) * a.q_s_token + (int64_t)(head0 + g) * a.q_s_head +
-                            c * 8);
-      else
-        *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+      if (tk < TQ && ti < nq && seq >= 0 && seq < a.num_seqs) {
+        p = a.pos[t0 + ti];
+        if (p >= 0 && (int64_t)((p + BS) / BS) > a.max_blocks) {
+          va::raise_flag(a.err, VA_FLAG_CTX_OVERFLOW);
+          p = -1;
+        }
+        if (p < 0) p = -1;
+      }
+      s_pos[tid] = p;
+      if (p >= 0) atomicMax(&s_ctx[h], p + 1);
     }
-    cp_async_commit();
-    cp_async_wait<0>();
-    va::fence_proxy_async_smem();
-    math_sync();
+    if (tid == 0) {
+      // every phase of the previous item has completed (its roles met at the end)
+      uint64_t *bars = bar_full;
+      constexpr int kBars = 2 * kStages + 5 * kTiles;
+      if (inited)
+        for (int i = 0; i < kBars; ++i) va::mbar_inval(&bars[i]);
+      for (int i = 0; i < kStages; ++i) {
+        va::mbar_init(&bar_full[i], 1);
+        va::mbar_init(&bar_empty[i], kTiles);
+      }
+      for (int i = 0; i < 2 * kTiles; ++i) va::mbar_init(&bar_s[i], 1);
+      for (int i = 0; i < kTiles; ++i) {
+        va::mbar_init(&bar_p[i], kRows);
+        va::mbar_init(&bar_pv[i], 1);
+        va::mbar_init(&bar_done[i], 1);
+      }
+      va::fence_barrier_init();
+      inited = true;
+    }
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
+    const int ctx = max(s_ctx[0], s_ctx[1]);
+    if (ctx == 0) continue;  // nothing to attend (all tokens skipped)
+    const int nch = (ctx + kKeys - 1) / kKeys;
+    const int32_t *bt_row = a.bt + (int64_t)seq * a.max_blocks;
 
-    if (warp > kProducerWarp) {
-      // =================== MMA issue for tile h (lane 0) ===================
-      const int h = warp - kMmaWarp;
-      const int nj = (s_ctx[h] + kKeys - 1) / kKeys;
-      const uint32_t sQ = va::smem_addr(smem + S::oQ) + h * S::kQ;
-      const uint32_t sK = va::smem_addr(smem + S::oK);
-      const uint32_t sV = va::smem_addr(smem + S::oV);
-      const uint32_t sP = va::smem_addr(smem + S::oP) + h * S::kP;
-      const uint32_t tS = tmem + 2 * h * kKeys;        // two S buffers of this tile
-      const uint32_t tO = tmem + 4 * kKeys + h * D;    // O of this tile
-      constexpr uint32_t IDESC_S = idesc_f16(kRows, kKeys, false);
-      constexpr uint32_t IDESC_O = idesc_f16(kRows, D, true);
-      auto wait_chunk = [&](int c) {
-        wait_bar(&bar_full[c % kStages], (uint32_t)((c / kStages) & 1));
+    if (warp == kProducerWarp) {
+      // =================== producer: K/V chunks into the stages ===================
+      const int npc = kKeys / BS;  // a power of two <= 8: a chunk never straddles a group
+      const int pages = (ctx + BS - 1) / BS;  // <= max_blocks (checked above)
+      const int tail_rows = ctx - (pages - 1) * BS;  // rows of the last page inside the context
+      // block ids are read 32 pages (one per lane) at a time, one group ahead
+      auto load_group = [&](int g) -> int32_t {
+        const int page = g * 32 + lane;
+        return page < pages ? __ldg(bt_row + page) : -1;
       };
-      // S_h(j) = Q_h K_j^T: A = Q_h [128 x D] K-major, B = K chunk [64 x D] K-major.
-      auto issue_s = [&](int j) {
-        if (lane == 0 && !dead()) {
-          fence_after_sync();
-          const uint32_t kbase = sK + (j % kStages) * S::kKV;
-#pragma unroll
-          for (int ks = 0; ks < D / 16; ++ks) {
-            const uint32_t kblk = ks >> 2, kin = (ks & 3) * 32;
-            umma_f16(tS + (j & 1) * kKeys, sdesc(sQ + kblk * kRows * 128 + kin, 16, 1024),
-                     sdesc(kbase + kblk * kKeys * 128 + kin, 16, 1024), IDESC_S, ks > 0);
+      int gi = 0;
+      int32_t g_cur = load_group(0), g_next = load_group(1);
+#pragma unroll 1
+      for (int c = 0; c < nch; ++c) {
+        const int buf = c % kStages;
+        const int first = c * npc;
+        if ((first >> 5) != gi) {
+          gi = first >> 5;
+          g_cur = g_next;
+          g_next = load_group(gi + 1);
+        }
+        const int32_t gid = __shfl_sync(0xffffffffu, g_cur, (first & 31) + (lane & (npc - 1)));
+        if (c >= kStages) wait_bar(&bar_empty[buf], (uint32_t)(((c / kStages) - 1) & 1));
+        // page ids of this chunk (lane p holds page p)
+        int32_t id = -1;
+        const int page = first + lane;
+        if (lane < npc && page < pages) {
+          id = gid;
+          if (id < 0 || id >= a.num_blocks) {
+            atomicMin(&s_bad_from, page * BS);
+            id = -2;
           }
-          umma_commit(&bar_s[2 * h + (j & 1)]);
+        }
+        unsigned char *kb = smem + S::oK + buf * S::kKV, *vb = smem + S::oV + buf * S::kKV;
+        // by TMA: valid whole pages; by the warp: the partial last page (copied, tail
+        // zeroed) and invalid / past-context pages (zeroed)
+        const bool part = page == pages - 1 && tail_rows < BS;
+        const unsigned valid = __ballot_sync(0xffffffffu, lane < npc && id >= 0 && !part);
+        const unsigned partial = __ballot_sync(0xffffffffu, lane < npc && id >= 0 && part);
+        if (valid != (1u << npc) - 1u) {  // only near the end of the context
+          const int ppage = partial ? __ffs(partial) - 1 : -1;
+          const int32_t pid = __shfl_sync(0xffffffffu, id, ppage < 0 ? 0 : ppage);
+          for (int i = lane; i < kKeys * CPR; i += 32) {
+            const int r = i / CPR, ch16 = i - r * CPR;
+            const int p = r / BS;
+            if ((valid >> p) & 1u) continue;
+            const uint32_t o = sw128_off(r, ch16 * 8, kKeys);
+            uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+            if (p == ppage && r - p * BS < tail_rows) {
+              const int64_t off = (int64_t)pid * a.s_block + (int64_t)kvh * a.s_head +
+                                  (int64_t)(r - p * BS) * a.s_token + ch16 * 8;
+              kv = __ldg(reinterpret_cast<const uint4 *>(a.kc + off));
+              vv = __ldg(reinterpret_cast<const uint4 *>(a.vc + off));
+            }
+            *reinterpret_cast<uint4 *>(kb + o) = kv;
+            *reinterpret_cast<uint4 *>(vb + o) = vv;
+          }
+          va::fence_proxy_async_smem();
+          __syncwarp();
+        }
+        if (lane == 0) va::mbar_arrive_expect_tx(&bar_full[buf], __popc(valid) * (2u * BS * D * 2u));
+        __syncwarp();
+        {  // one box per lane: lane = (page, 64-column block, K or V)
+          constexpr int kBoxes = D / 64 * 2;
+          const int p = lane / kBoxes, rem = lane - p * kBoxes;
+          const int kbk = rem >> 1;
+          const int pidl = __shfl_sync(0xffffffffu, id, p & 31);
+          if (p < npc && ((valid >> p) & 1u)) {
+            const uint32_t off = kbk * kKeys * 128 + p * BS * 128;
+            const int c1 = a.nhd ? kvh : 0;
+            const int c2 = a.nhd ? pidl * BS : pidl * a.Hkv + kvh;
+            if (rem & 1)
+              tma_load_3d(vb + off, &tmv, kbk * 64, c1, c2, &bar_full[buf]);
+            else
+              tma_load_3d(kb + off, &tmk, kbk * 64, c1, c2, &bar_full[buf]);
+          }
         }
         __syncwarp();
-      };
-      // O_h (+)= P_h V_j: A = P_h [128 x 64] K-major, B = V chunk [64 keys x D] MN-major
-      // (LBO = next 64 columns, SBO = next 8 keys).
-      auto issue_pv = [&](int j) {
-        wait_bar(&bar_p[h], (uint32_t)(j & 1));
-        if (lane == 0 && !dead()) {
-          fence_after_sync();
-          const uint32_t vbase = sV + (j % kStages) * S::kKV;
-#pragma unroll
-          for (int ks = 0; ks < kKeys / 16; ++ks)
-            umma_f16(tO, sdesc(sP + ks * 32, 16, 1024),
-                     sdesc(vbase + ks * 2048, kKeys * 128, 1024), IDESC_O,
-                     (j > 0 || ks > 0) ? 1u : 0u);
-          umma_commit(&bar_pv[h]);
-        }
-        __syncwarp();
-      };
-      // S runs two chunks ahead of PV: S_h(j+2) reuses the buffer of S_h(j), read
-      // before P_h(j) was published.  Every chunk is waited for (and released) by
-      // both MMA warps, also past this tile's context, so the stage barriers stay
-      // in step.
-#pragma unroll 1
-      for (int c = 0; c < 2 && c < nch; ++c) {
-        wait_chunk(c);
-        if (c < nj) issue_s(c);
+        if (dead()) break;
       }
-#pragma unroll 1
-      for (int j = 0; j < nch; ++j) {
-        if (j < nj) issue_pv(j);
-        // stage j is free once PV(j) (and S(j), issued earlier) completes: release it
-        // before S(j+2) goes in, so the producer's refill is not held behind it
-        if (lane == 0 && !dead()) umma_commit(&bar_empty[j % kStages]);
-        __syncwarp();
-        if (j + 2 < nch) {
-          wait_chunk(j + 2);
-          if (j + 2 < nj) issue_s(j + 2);
-        }
-      }
-      // teardown: every MMA issued by this thread has retired
+      // no copy may still be landing when the CTA exits (normally none is: the
+      // MMA warps consumed every chunk); bounded, reports like any other wait
       if (lane == 0) {
-        umma_commit(&bar_done[h]);
-        if (!va::mbar_wait_bounded(&bar_done[h], 0, kWaitLimit)) timeout();
+        for (int c = nch - kStages < 0 ? 0 : nch - kStages; c < nch; ++c)
+          if (!va::mbar_wait_bounded(&bar_full[c % kStages], (uint32_t)((c / kStages) & 1),
+                                     kWaitLimit))
+            timeout();
       }
       __syncwarp();
       all_sync();
     } else {
-      // =================== softmax of tile h, one thread per row ===================
-      const int h = warp >> 2;
-      const int row = tid & (kRows - 1);
-      const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-      const uint32_t tO = tmem + 4 * kKeys + h * D + lane_base;
-      const int tk = row / GC;
-      const int my_pos = (tk < TQ) ? s_pos[h * kRows + tk] : -1;
-      const int nj = (s_ctx[h] + kKeys - 1) / kKeys;
-      unsigned char *prow = smem + S::oP + h * S::kP;
-      // m: the max the probabilities are taken against.  It only moves when the row
-      // max exceeds it by more than 2^8 (P stays <= 256, exact enough in fp16, and
-      // O / l at the end cancels it), so O is rescaled in TMEM rarely.
-      float m = -INFINITY, l = 0.f;
-#pragma unroll 1
-      for (int j = 0; j < nj; ++j) {
-        float p[kKeys];
-        {
-          wait_bar(&bar_s[2 * h + (j & 1)], (uint32_t)((j >> 1) & 1));
-          fence_after_sync();
-          uint32_t sr[32];
-          const uint32_t tS = tmem + (2 * h + (j & 1)) * kKeys + lane_base;
-          tmem_ld32(tS, sr);
-          tmem_wait_ld();
+      // ---- Q of both tiles: cp.async by the softmax and MMA warps ----
+      const int mtid = warp > kProducerWarp ? tid - 32 : tid;  // 0 .. kMath - 1
+      for (int i = mtid; i < kTiles * kRows * CPR; i += kMath) {
+        const int r2 = i / CPR, c = i - r2 * CPR;
+        const int h = r2 / kRows, r = r2 - h * kRows;
+        const int tk = r / GC, g = r - tk * GC;
+        const int ti = h * TQ + tk;
+        unsigned char *dst = smem + S::oQ + h * S::kQ + sw128_off(r, c * 8, kRows);
+        if (tk < TQ && ti < nq)
+          cp_async16(dst, a.q + (int64_t)(t0 + ti) * a.q_s_token + (int64_t)(head0 + g) * a.q_s_head +
+                              c * 8);
+        else
+          *reinterpret_cast<uint4 *>(dst) = make_uint4(0, 0, 0, 0);
+      }
+      cp_async_commit();
+      cp_async_wait<0>();
+      va::fence_proxy_async_smem();
+      math_sync();
+
+      if (warp > kProducerWarp) {
+        // =================== MMA issue for tile h (lane 0) ===================
+        const int h = warp - kMmaWarp;
+        const int nj = (s_ctx[h] + kKeys - 1) / kKeys;
+        const uint32_t sQ = va::smem_addr(smem + S::oQ) + h * S::kQ;
+        const uint32_t sK = va::smem_addr(smem + S::oK);
+        const uint32_t sV = va::smem_addr(smem + S::oV);
+        const uint32_t sP = va::smem_addr(smem + S::oP) + h * S::kP;
+        const uint32_t tS = tmem + 2 * h * kKeys;        // two S buffers of this tile
+        const uint32_t tO = tmem + 4 * kKeys + h * D;    // O of this tile
+        constexpr uint32_t IDESC_S = idesc_f16(kRows, kKeys, false);
+        constexpr uint32_t IDESC_O = idesc_f16(kRows, D, true);
+        auto wait_chunk = [&](int c) {
+          wait_bar(&bar_full[c % kStages], (uint32_t)((c / kStages) & 1));
+        };
+        // S_h(j) = Q_h K_j^T: A = Q_h [128 x D] K-major, B = K chunk [64 x D] K-major.
+        auto issue_s = [&](int j) {
+          if (lane == 0 && !dead()) {
+            fence_after_sync();
+            const uint32_t kbase = sK + (j % kStages) * S::kKV;
 #pragma unroll
-          for (int c = 0; c < 32; ++c) p[c] = __uint_as_float(sr[c]);
-          tmem_ld32(tS + 32, sr);
-          tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 32; ++c) p[32 + c] = __uint_as_float(sr[c]);
-        }
-        float alpha;
-        {
-          // raw scores: the scale (> 0) is applied in the exponent's FMA
-          const int vis = my_pos - j * kKeys;  // keys 0..vis of this chunk are visible
-          if (vis < kKeys - 1) {
-#pragma unroll
-            for (int c = 0; c < kKeys; ++c) p[c] = c <= vis ? p[c] : -INFINITY;
-          }
-          float mx4[4] = {p[0], p[1], p[2], p[3]};
-#pragma unroll
-          for (int c = 4; c < kKeys; c += 8) {
-            mx4[0] = fmax3(mx4[0], p[c + 0], p[c + 1]);
-            mx4[1] = fmax3(mx4[1], p[c + 2], p[c + 3]);
-            mx4[2] = fmax3(mx4[2], p[c + 4], p[c + 5]);
-            if (c + 7 < kKeys) mx4[3] = fmax3(mx4[3], p[c + 6], p[c + 7]);
-            else mx4[3] = fmaxf(mx4[3], p[c + 6]);
-          }
-          const float rmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
-          const float mn = (m == -INFINITY || rmax > m + 8.f) ? fmaxf(m, rmax) : m;
-          const bool none = mn == -INFINITY;
-          alpha = (none || mn == m) ? 1.f : va::fast_exp2(m - mn);
-          const float nmn = none ? 0.f : -mn;
-          // p = 2^(s * scale - m) in pairs; every third pair on the FMA pipe (the
-          // special-function unit is the softmax's bottleneck)
-          const uint64_t sc2 = pk2(a.scale_log2, a.scale_log2), nm2 = pk2(nmn, nmn);
-          uint64_t sum2[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)};
-#pragma unroll
-          for (int c = 0; c < kKeys / 2; ++c) {
-            const uint64_t x = ffma2(pk2(p[2 * c], p[2 * c + 1]), sc2, nm2);
-            uint64_t e;
-            if (c % 3 == 2) {
-              e = exp2_poly2(x);
-            } else {
-              float x0, x1;
-              upk2(x, x0, x1);
-              e = pk2(va::fast_exp2(x0), va::fast_exp2(x1));
+            for (int ks = 0; ks < D / 16; ++ks) {
+              const uint32_t kblk = ks >> 2, kin = (ks & 3) * 32;
+              umma_f16(tS + (j & 1) * kKeys, sdesc(sQ + kblk * kRows * 128 + kin, 16, 1024),
+                       sdesc(kbase + kblk * kKeys * 128 + kin, 16, 1024), IDESC_S, ks > 0);
             }
-            upk2(e, p[2 * c], p[2 * c + 1]);
-            sum2[c & 1] = fadd2(sum2[c & 1], e);
+            umma_commit(&bar_s[2 * h + (j & 1)]);
           }
-          float s0, s1, s2, s3;
-          upk2(sum2[0], s0, s1);
-          upk2(sum2[1], s2, s3);
-          l = l * alpha + ((s0 + s1) + (s2 + s3));
-          m = mn;
+          __syncwarp();
+        };
+        // O_h (+)= P_h V_j: A = P_h [128 x 64] K-major, B = V chunk [64 keys x D] MN-major
+        // (LBO = next 64 columns, SBO = next 8 keys).
+        auto issue_pv = [&](int j) {
+          wait_bar(&bar_p[h], (uint32_t)(j & 1));
+          if (lane == 0 && !dead()) {
+            fence_after_sync();
+            const uint32_t vbase = sV + (j % kStages) * S::kKV;
+#pragma unroll
+            for (int ks = 0; ks < kKeys / 16; ++ks)
+              umma_f16(tO, sdesc(sP + ks * 32, 16, 1024),
+                       sdesc(vbase + ks * 2048, kKeys * 128, 1024), IDESC_O,
+                       (j > 0 || ks > 0) ? 1u : 0u);
+            umma_commit(&bar_pv[h]);
+          }
+          __syncwarp();
+        };
+        // S runs two chunks ahead of PV: S_h(j+2) reuses the buffer of S_h(j), read
+        // before P_h(j) was published.  Every chunk is waited for (and released) by
+        // both MMA warps, also past this tile's context, so the stage barriers stay
+        // in step.
+#pragma unroll 1
+        for (int c = 0; c < 2 && c < nch; ++c) {
+          wait_chunk(c);
+          if (c < nj) issue_s(c);
         }
-        // PV_h(j-1) done: P_h and O_h are free
-        if (j > 0) {
-          wait_bar(&bar_pv[h], (uint32_t)((j - 1) & 1));
+#pragma unroll 1
+        for (int j = 0; j < nch; ++j) {
+          if (j < nj) issue_pv(j);
+          // stage j is free once PV(j) (and S(j), issued earlier) completes: release it
+          // before S(j+2) goes in, so the producer's refill is not held behind it
+          if (lane == 0 && !dead()) umma_commit(&bar_empty[j % kStages]);
+          __syncwarp();
+          if (j + 2 < nch) {
+            wait_chunk(j + 2);
+            if (j + 2 < nj) issue_s(j + 2);
+          }
+        }
+        // teardown: every MMA issued by this thread has retired
+        if (lane == 0) {
+          umma_commit(&bar_done[h]);
+          if (!va::mbar_wait_bounded(&bar_done[h], 0, kWaitLimit)) timeout();
+        }
+        __syncwarp();
+        all_sync();
+      } else {
+        // =================== softmax of tile h, one thread per row ===================
+        const int h = warp >> 2;
+        const int row = tid & (kRows - 1);
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t tO = tmem + 4 * kKeys + h * D + lane_base;
+        const int tk = row / GC;
+        const int my_pos = (tk < TQ) ? s_pos[h * kRows + tk] : -1;
+        const int nj = (s_ctx[h] + kKeys - 1) / kKeys;
+        unsigned char *prow = smem + S::oP + h * S::kP;
+        // m: the max the probabilities are taken against.  It only moves when the row
+        // max exceeds it by more than 2^8 (P stays <= 256, exact enough in fp16, and
+        // O / l at the end cancels it), so O is rescaled in TMEM rarely.
+        float m = -INFINITY, l = 0.f;
+#pragma unroll 1
+        for (int j = 0; j < nj; ++j) {
+          float p[kKeys];
+          {
+            wait_bar(&bar_s[2 * h + (j & 1)], (uint32_t)((j >> 1) & 1));
+            fence_after_sync();
+            uint32_t sr[32];
+            const uint32_t tS = tmem + (2 * h + (j & 1)) * kKeys + lane_base;
+            tmem_ld32(tS, sr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) p[c] = __uint_as_float(sr[c]);
+            tmem_ld32(tS + 32, sr);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) p[32 + c] = __uint_as_float(sr[c]);
+          }
+          float alpha;
+          {
+            // raw scores: the scale (> 0) is applied in the exponent's FMA
+            const int vis = my_pos - j * kKeys;  // keys 0..vis of this chunk are visible
+            if (vis < kKeys - 1) {
+#pragma unroll
+              for (int c = 0; c < kKeys; ++c) p[c] = c <= vis ? p[c] : -INFINITY;
+            }
+            float mx4[4] = {p[0], p[1], p[2], p[3]};
+#pragma unroll
+            for (int c = 4; c < kKeys; c += 8) {
+              mx4[0] = fmax3(mx4[0], p[c + 0], p[c + 1]);
+              mx4[1] = fmax3(mx4[1], p[c + 2], p[c + 3]);
+              mx4[2] = fmax3(mx4[2], p[c + 4], p[c + 5]);
+              if (c + 7 < kKeys) mx4[3] = fmax3(mx4[3], p[c + 6], p[c + 7]);
+              else mx4[3] = fmaxf(mx4[3], p[c + 6]);
+            }
+            const float rmax = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
+            const float mn = (m == -INFINITY || rmax > m + 8.f) ? fmaxf(m, rmax) : m;
+            const bool none = mn == -INFINITY;
+            alpha = (none || mn == m) ? 1.f : va::fast_exp2(m - mn);
+            const float nmn = none ? 0.f : -mn;
+            // p = 2^(s * scale - m) in pairs; every third pair on the FMA pipe (the
+            // special-function unit is the softmax's bottleneck)
+            const uint64_t sc2 = pk2(a.scale_log2, a.scale_log2), nm2 = pk2(nmn, nmn);
+            uint64_t sum2[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)};
+#pragma unroll
+            for (int c = 0; c < kKeys / 2; ++c) {
+              const uint64_t x = ffma2(pk2(p[2 * c], p[2 * c + 1]), sc2, nm2);
+              uint64_t e;
+              if (c % 3 == 2) {
+                e = exp2_poly2(x);
+              } else {
+                float x0, x1;
+                upk2(x, x0, x1);
+                e = pk2(va::fast_exp2(x0), va::fast_exp2(x1));
+              }
+              upk2(e, p[2 * c], p[2 * c + 1]);
+              sum2[c & 1] = fadd2(sum2[c & 1], e);
+            }
+            float s0, s1, s2, s3;
+            upk2(sum2[0], s0, s1);
+            upk2(sum2[1], s2, s3);
+            l = l * alpha + ((s0 + s1) + (s2 + s3));
+            m = mn;
+          }
+          // PV_h(j-1) done: P_h and O_h are free
+          if (j > 0) {
+            wait_bar(&bar_pv[h], (uint32_t)((j - 1) & 1));
+            fence_after_sync();
+          }
+          // rescale this row of O where the max moved (warp-collective TMEM access)
+          if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+            for (int c = 0; c < D; c += 32) {
+              uint32_t o[32];
+              tmem_ld32(tO + c, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+              tmem_st32(tO + c, o);
+            }
+            tmem_wait_st();
+          }
+          // P row (fp16, swizzled), then publish it to the MMA warp
+#pragma unroll
+          for (int c = 0; c < kKeys / 8; ++c) {
+            uint4 w;
+            w.x = va::pack_h2(p[8 * c + 0], p[8 * c + 1]);
+            w.y = va::pack_h2(p[8 * c + 2], p[8 * c + 3]);
+            w.z = va::pack_h2(p[8 * c + 4], p[8 * c + 5]);
+            w.w = va::pack_h2(p[8 * c + 6], p[8 * c + 7]);
+            *reinterpret_cast<uint4 *>(prow + sw128_off(row, c * 8, kRows)) = w;
+          }
+          va::fence_proxy_async_smem();
+          fence_before_sync();
+          va::mbar_arrive(&bar_p[h]);
+        }
+        if (nj > 0) {
+          wait_bar(&bar_pv[h], (uint32_t)((nj - 1) & 1));
           fence_after_sync();
         }
-        // rescale this row of O where the max moved (warp-collective TMEM access)
-        if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // ---- epilogue: O / l -> fp16 rows, once every role is done ----
+        all_sync();  // s_bad_from / s_dead are final
+        const bool ok = !dead();  // uniform across the CTA after the barrier
+        const int bad_from = s_bad_from;
+        if (bad_from != INT_MAX && tid == 0) va::raise_flag(a.err, VA_FLAG_BAD_BLOCK);
+        const int ti = h * TQ + tk;
+        const bool write = ok && nj > 0 && my_pos >= 0 && my_pos < bad_from && tk < TQ && ti < nq &&
+                           row < TQ * GC;
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const int g = row - tk * GC;
+        __half *orow = a.out + (int64_t)(t0 + ti) * a.o_s_token + (int64_t)(head0 + g) * a.o_s_head;
+        if (ok && nj > 0) {
 #pragma unroll 1
           for (int c = 0; c < D; c += 32) {
             uint32_t o[32];
             tmem_ld32(tO + c, o);
             tmem_wait_ld();
+            if (write) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(tO + c, o);
-          }
-          tmem_wait_st();
-        }
-        // P row (fp16, swizzled), then publish it to the MMA warp
-#pragma unroll
-        for (int c = 0; c < kKeys / 8; ++c) {
-          uint4 w;
-          w.x = va::pack_h2(p[8 * c + 0], p[8 * c + 1]);
-          w.y = va::pack_h2(p[8 * c + 2], p[8 * c + 3]);
-          w.z = va::pack_h2(p[8 * c + 4], p[8 * c + 5]);
-          w.w = va::pack_h2(p[8 * c + 6], p[8 * c + 7]);
-          *reinterpret_cast<uint4 *>(prow + sw128_off(row, c * 8, kRows)) = w;
-        }
-        va::fence_proxy_async_smem();
-        fence_before_sync();
-        va::mbar_arrive(&bar_p[h]);
-      }
-      if (nj > 0) {
-        wait_bar(&bar_pv[h], (uint32_t)((nj - 1) & 1));
-        fence_after_sync();
-      }
-      // ---- epilogue: O / l -> fp16 rows, once every role is done ----
-      all_sync();  // s_bad_from / s_dead are final
-      const bool ok = !dead();  // uniform across the CTA after the barrier
-      const int bad_from = s_bad_from;
-      if (bad_from != INT_MAX && tid == 0) va::raise_flag(a.err, VA_FLAG_BAD_BLOCK);
-      const int ti = h * TQ + tk;
-      const bool write = ok && nj > 0 && my_pos >= 0 && my_pos < bad_from && tk < TQ && ti < nq &&
-                         row < TQ * GC;
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      const int g = row - tk * GC;
-      __half *orow = a.out + (int64_t)(t0 + ti) * a.o_s_token + (int64_t)(head0 + g) * a.o_s_head;
-      if (ok && nj > 0) {
-#pragma unroll 1
-        for (int c = 0; c < D; c += 32) {
-          uint32_t o[32];
-          tmem_ld32(tO + c, o);
-          tmem_wait_ld();
-          if (write) {
-#pragma unroll
-            for (int i = 0; i < 32; i += 8) {
-              uint4 w;
-              w.x = va::pack_h2(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
-              w.y = va::pack_h2(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
-              w.z = va::pack_h2(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
-              w.w = va::pack_h2(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
-              *reinterpret_cast<uint4 *>(orow + c + i) = w;
+              for (int i = 0; i < 32; i += 8) {
+                uint4 w;
+                w.x = va::pack_h2(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
+                w.y = va::pack_h2(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+                w.z = va::pack_h2(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
+                w.w = va::pack_h2(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
+                *reinterpret_cast<uint4 *>(orow + c + i) = w;
+              }
             }
           }
         }
       }
     }
+    // all roles meet here before the next item re-initialises the barriers
+    fence_before_sync();
+    __syncthreads();
+    fence_after_sync();
   }
-  // all roles meet here; the first MMA warp releases TMEM
+  // the first MMA warp releases TMEM
   fence_before_sync();
   __syncthreads();
   if (warp == kMmaWarp) {
