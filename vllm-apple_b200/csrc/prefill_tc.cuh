@@ -19,13 +19,17 @@
 //     the page holding the end of the context is copied row by row with its
 //     tail zeroed (V rows past the context must not hold NaN: P = 0 there).
 //   * Warp 9 + h (MMA for tile h) issues S_h = Q_h K^T (M=128, N=64, K=D) two
-//     chunks ahead into one of two TMEM buffers, and O_h += P_h V (V as an
-//     MN-major operand: the same shared-memory image as K) once warpgroup h
-//     has published P_h.  One issuing warp per tile: neither tile waits for
-//     the other's softmax; a stage is free when both warps committed it.
+//     chunks ahead into one of two TMEM buffers, and O_h += P_h V once warpgroup
+//     h has written P_h (fp16) over the first 32 columns of that chunk's S
+//     buffer: A is read from TMEM (the tcgen05.mma [a_tmem] form), B = V as an
+//     MN-major operand (the same shared-memory image as K).  Keeping P out of
+//     shared memory matters: the UMMA operand reads, the TMA writes and the P
+//     stores all share the SM's 128 B/clk of shared-memory bandwidth.  One
+//     issuing warp per tile: neither tile waits for the other's softmax; a
+//     stage is free when both warps committed it.
 //   * Softmax: log2-domain online softmax; the max only moves when it grows by
-//     more than 2^8, so O is rarely rescaled in TMEM.  P (fp16) goes to shared
-//     memory in the swizzled K-major layout.
+//     more than 2^8, so O is rarely rescaled in TMEM (only then does the
+//     softmax wait for the previous PV).
 //   * Q is staged once by cp.async from the softmax and MMA warps, while the
 //     producer already streams the first chunks.
 //   * Every wait on an mbarrier is bounded and reports VA_FLAG_WAIT_TIMEOUT;
@@ -48,7 +52,7 @@ constexpr int kMath = kSoftmax + 32 * kTiles;  // softmax + MMA threads
 constexpr int kThreads = kMath + 32;           // + producer warp
 constexpr uint32_t kTmemCols = 512;  // S: 2 tiles x 2 buffers x 64; O: 2 tiles x D (<= 128)
 constexpr uint32_t kWaitLimit = 1u << 22;
-constexpr int kStages = 4;  // K/V chunks in flight (a chunk = 64 keys of K and of V)
+constexpr int kStages = 5;  // K/V chunks in flight (a chunk = 64 keys of K and of V)
 
 // ---- PTX wrappers (tcgen05 family, sm_100a) --------------------------------
 VA_DEVINL void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {  // whole warp
@@ -75,6 +79,17 @@ VA_DEVINL void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A[tmem] * B[smem desc]: A (M x K fp16, K-major) read from TMEM, one
+// row per lane, two fp16 per 32-bit column (K = 16 per instruction: 8 columns).
+VA_DEVINL void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // Arrive on `bar` once every MMA issued so far by this thread has completed.
@@ -232,10 +247,8 @@ template <int D>
 struct Smem {
   static constexpr uint32_t kQ = kRows * D * 2;      // 16/32 KB per tile
   static constexpr uint32_t kKV = kKeys * D * 2;     // 8/16 KB per chunk
-  static constexpr uint32_t kP = kRows * kKeys * 2;  // 16 KB per tile
   static constexpr uint32_t oQ = 0, oK = kTiles * kQ, oV = oK + kStages * kKV,
-                            oP = oV + kStages * kKV;
-  static constexpr uint32_t oBar = oP + kTiles * kP;  // mbarriers + tmem slot
+                            oBar = oV + kStages * kKV;  // mbarriers + tmem slot
   static constexpr uint32_t oPos = oBar + 256;        // int [kTiles][kRows]
   static constexpr uint32_t kBytes = oPos + kTiles * kRows * 4 + 1024;  // + 1 KB alignment slack
 };
@@ -429,13 +442,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (dead()) break;
       }
-      // no copy may still be landing when the CTA exits (normally none is: the
-      // MMA warps consumed every chunk); bounded, reports like any other wait
+      // Before the barriers are re-initialised for the next item, nothing may still
+      // arrive on them: no copy may still be landing (normally none is: the MMA
+      // warps consumed every chunk), and the stage releases the MMA warps commit
+      // for the last chunks -- which nobody else waits for -- must have arrived.
+      // Bounded, reported like any other wait.
       if (lane == 0) {
-        for (int c = nch - kStages < 0 ? 0 : nch - kStages; c < nch; ++c)
-          if (!va::mbar_wait_bounded(&bar_full[c % kStages], (uint32_t)((c / kStages) & 1),
-                                     kWaitLimit))
+        for (int c = nch - kStages < 0 ? 0 : nch - kStages; c < nch; ++c) {
+          const uint32_t par = (uint32_t)((c / kStages) & 1);
+          if (!va::mbar_wait_bounded(&bar_full[c % kStages], par, kWaitLimit)) timeout();
+          if (!dead() && !va::mbar_wait_bounded(&bar_empty[c % kStages], par, kWaitLimit))
             timeout();
+        }
       }
       __syncwarp();
       all_sync();
@@ -466,7 +484,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t sQ = va::smem_addr(smem + S::oQ) + h * S::kQ;
         const uint32_t sK = va::smem_addr(smem + S::oK);
         const uint32_t sV = va::smem_addr(smem + S::oV);
-        const uint32_t sP = va::smem_addr(smem + S::oP) + h * S::kP;
         const uint32_t tS = tmem + 2 * h * kKeys;        // two S buffers of this tile
         const uint32_t tO = tmem + 4 * kKeys + h * D;    // O of this tile
         constexpr uint32_t IDESC_S = idesc_f16(kRows, kKeys, false);
@@ -489,8 +506,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           __syncwarp();
         };
-        // O_h (+)= P_h V_j: A = P_h [128 x 64] K-major, B = V chunk [64 keys x D] MN-major
-        // (LBO = next 64 columns, SBO = next 8 keys).
+        // O_h (+)= P_h V_j: A = P_h [128 x 64] from TMEM (written by the softmax over the
+        // first 32 columns of S_h(j)'s buffer), B = V chunk [64 keys x D] MN-major
+        // (LBO = next 64 columns, SBO = next 8 keys).  S_h(j+2), issued later by this
+        // thread into the same buffer, executes after this MMA has read P (one
+        // thread's tcgen05.mma operations run in issue order).
         auto issue_pv = [&](int j) {
           wait_bar(&bar_p[h], (uint32_t)(j & 1));
           if (lane == 0 && !dead()) {
@@ -498,9 +518,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t vbase = sV + (j % kStages) * S::kKV;
 #pragma unroll
             for (int ks = 0; ks < kKeys / 16; ++ks)
-              umma_f16(tO, sdesc(sP + ks * 32, 16, 1024),
-                       sdesc(vbase + ks * 2048, kKeys * 128, 1024), IDESC_O,
-                       (j > 0 || ks > 0) ? 1u : 0u);
+              umma_f16_ts(tO, tmem + (2 * h + (j & 1)) * kKeys + ks * 8,
+                          sdesc(vbase + ks * 2048, kKeys * 128, 1024), IDESC_O,
+                          (j > 0 || ks > 0) ? 1u : 0u);
             umma_commit(&bar_pv[h]);
           }
           __syncwarp();
@@ -542,7 +562,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tk = row / GC;
         const int my_pos = (tk < TQ) ? s_pos[h * kRows + tk] : -1;
         const int nj = (s_ctx[h] + kKeys - 1) / kKeys;
-        unsigned char *prow = smem + S::oP + h * S::kP;
         // m: the max the probabilities are taken against.  It only moves when the row
         // max exceeds it by more than 2^8 (P stays <= 256, exact enough in fp16, and
         // O / l at the end cancels it), so O is rescaled in TMEM rarely.
@@ -610,13 +629,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             l = l * alpha + ((s0 + s1) + (s2 + s3));
             m = mn;
           }
-          // PV_h(j-1) done: P_h and O_h are free
-          if (j > 0) {
+          // rescale this row of O where the max moved (warp-collective TMEM access),
+          // once PV_h(j-1) is done with O.  P_h(j) goes to S_h(j)'s own buffer, which
+          // no pending MMA reads, so without a rescale there is nothing to wait for.
+          if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
             wait_bar(&bar_pv[h], (uint32_t)((j - 1) & 1));
             fence_after_sync();
-          }
-          // rescale this row of O where the max moved (warp-collective TMEM access)
-          if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
             for (int c = 0; c < D; c += 32) {
               uint32_t o[32];
@@ -628,17 +646,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             tmem_wait_st();
           }
-          // P row (fp16, swizzled), then publish it to the MMA warp
+          // P row (fp16 pairs) into the first 32 columns of S_h(j)'s TMEM buffer (already
+          // read above), then publish it to the MMA warp
+          {
+            uint32_t pw[32];
 #pragma unroll
-          for (int c = 0; c < kKeys / 8; ++c) {
-            uint4 w;
-            w.x = va::pack_h2(p[8 * c + 0], p[8 * c + 1]);
-            w.y = va::pack_h2(p[8 * c + 2], p[8 * c + 3]);
-            w.z = va::pack_h2(p[8 * c + 4], p[8 * c + 5]);
-            w.w = va::pack_h2(p[8 * c + 6], p[8 * c + 7]);
-            *reinterpret_cast<uint4 *>(prow + sw128_off(row, c * 8, kRows)) = w;
+            for (int c = 0; c < 32; ++c) pw[c] = va::pack_h2(p[2 * c], p[2 * c + 1]);
+            tmem_st32(tmem + (2 * h + (j & 1)) * kKeys + lane_base, pw);
+            tmem_wait_st();
           }
-          va::fence_proxy_async_smem();
           fence_before_sync();
           va::mbar_arrive(&bar_p[h]);
         }
