@@ -2,9 +2,9 @@
 // (tcgen05 UMMA, TMEM accumulators), head_size 64 or 128.  Included by
 // paged_prefill.cu, which owns the tile planner and the C-ABI entry point.
 //
-// One CTA per (tile pair, kv head [, q-head group]); 11 warps with fixed roles.
-// CTAs are launched longest context first (the planner orders the tiles), so
-// the long tiles of every sequence and head start in the first wave.
+// Persistent CTAs (one per SM: shared memory and TMEM allow no more) take
+// items = (tile pair, kv head [, q-head group]) from a counter in the planner's
+// order, longest context first; 11 warps with fixed roles per item.
 //   * A tile = 128 MMA rows = (token, q head) pairs of up to 128/G consecutive
 //     tokens of one sequence; a CTA owns two consecutive tiles of the same
 //     sequence, so every staged K/V chunk serves both tiles and every head of
@@ -30,8 +30,10 @@
 //   * Softmax: log2-domain online softmax; the max only moves when it grows by
 //     more than 2^8, so O is rarely rescaled in TMEM (only then does the
 //     softmax wait for the previous PV).
-//   * Q is staged once by cp.async from the softmax and MMA warps, while the
-//     producer already streams the first chunks.
+//   * Q is staged once per item by cp.async from the softmax and MMA warps, while
+//     the producer already streams the first chunks.  TMEM is allocated once per
+//     CTA; the mbarriers are re-initialised between items, after every arrival
+//     of the previous item has landed.
 //   * Every wait on an mbarrier is bounded and reports VA_FLAG_WAIT_TIMEOUT;
 //     after a timeout the CTA runs to the end without waiting or issuing,
 //     waits (bounded) for its copies and MMAs in flight and frees TMEM.
