@@ -201,6 +201,9 @@ __global__ void __launch_bounds__(kNW * 32, decode_min_blocks<D, GC>())
   float *pbuf = reinterpret_cast<float *>(smem + C::kStageBytes + C::kBarBytes);
   float *abuf = pbuf + kNW * BS * GP;
 
+  // the combine kernel (launched with programmatic dependency) may be scheduled now;
+  // it waits for this grid's completion before reading any partial
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int seq = blockIdx.z;  // index of the partials; = the sequence outside row mode
   int bt_seq, L_in;
   int64_t qo;
@@ -517,6 +520,9 @@ VA_DEVINL int64_t seq_splits(const DecodeArgs &a, int L_in, int bs, int grid_spl
 template <int D>
 __global__ void __launch_bounds__(1024) paged_decode_combine_kernel(const DecodeArgs a, int gc,
                                                                     int bs) {
+  // launched as a programmatic dependent of the split kernel: wait until that grid
+  // has completed and its partials are visible
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int seq = blockIdx.x;
   int bt_seq, L_in;
   int64_t qo;
@@ -648,7 +654,20 @@ int launch_t(const DecodeArgs &a, dim3 grid, cudaStream_t st) {
   if (grid.x > 1) {
     const int st0 = va_host::launch_status();
     if (st0 != VA_OK) return st0;
-    paged_decode_combine_kernel<D><<<dim3(grid.z, grid.y), GC * D, 0, st>>>(a, GC, BS);
+    // programmatic dependent launch: the combine grid's launch overlaps the split
+    // kernel's tail instead of following its completion
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid.z, grid.y);
+    cfg.blockDim = dim3(GC * D);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, paged_decode_combine_kernel<D>, a, GC, BS) != cudaSuccess)
+      return VA_ERR_LAUNCH;
   }
   return va_host::launch_status();
 }
