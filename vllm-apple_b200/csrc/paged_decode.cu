@@ -88,6 +88,17 @@ VA_DEVINL bool decode_row(const DecodeArgs &a, int r, int bs, int &bt_seq, int &
 
 constexpr int pow2ceil(int x) { return x <= 1 ? 1 : 2 * pow2ceil((x + 1) / 2); }
 
+// acc[0..1] = fma(p, v[0..1], acc[0..1]) as one packed sm_100 f32x2 FMA (each lane
+// rounded exactly like fmaf).
+VA_DEVINL void ffma2_bcast(float &a0, float &a1, float p, float v0, float v1) {
+  uint64_t acc, vv, pp;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(acc) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(vv) : "f"(v0), "f"(v1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(pp) : "f"(p));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(pp), "l"(vv));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(acc));
+}
+
 template <int D>
 struct Shape {
   static constexpr int DPL = (D == 96) ? 24 : (D == 128 ? VA_DECODE_DPL128 : 16);  // dims per lane in QK^T
@@ -435,9 +446,16 @@ __global__ void __launch_bounds__(kNW * 32, decode_min_blocks<D, GC>())
           p[0] = pr[0];
         }
 #pragma unroll
-        for (int h = 0; h < GC; ++h)
+        for (int h = 0; h < GC; ++h) {
+          if constexpr (DV % 2 == 0) {
 #pragma unroll
-          for (int j = 0; j < DV; ++j) acc[h][j] = fmaf(p[h], v[j], acc[h][j]);
+            for (int j = 0; j < DV; j += 2)
+              ffma2_bcast(acc[h][j], acc[h][j + 1], p[h], v[j], v[j + 1]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < DV; ++j) acc[h][j] = fmaf(p[h], v[j], acc[h][j]);
+          }
+        }
       };
       if (ntok == BS) {
 #pragma unroll
