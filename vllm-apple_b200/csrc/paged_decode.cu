@@ -88,6 +88,15 @@ VA_DEVINL bool decode_row(const DecodeArgs &a, int r, int bs, int &bt_seq, int &
 
 constexpr int pow2ceil(int x) { return x <= 1 ? 1 : 2 * pow2ceil((x + 1) / 2); }
 
+// a[0..1] *= s as one packed f32x2 multiply (each lane rounded like a fp32 multiply).
+VA_DEVINL void fmul2_bcast(float &a0, float &a1, float sc) {
+  uint64_t acc, ss;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(acc) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(ss) : "f"(sc));
+  asm("mul.rn.f32x2 %0, %0, %1;" : "+l"(acc) : "l"(ss));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(acc));
+}
+
 // acc[0..1] = fma(p, v[0..1], acc[0..1]) as one packed sm_100 f32x2 FMA (each lane
 // rounded exactly like fmaf).
 VA_DEVINL void ffma2_bcast(float &a0, float &a1, float p, float v0, float v1) {
@@ -425,9 +434,15 @@ __global__ void __launch_bounds__(kNW * 32, decode_min_blocks<D, GC>())
 #pragma unroll
       for (int h = 0; h < GC; ++h) al[h] = aw[h];
 #pragma unroll
-      for (int h = 0; h < GC; ++h)
+      for (int h = 0; h < GC; ++h) {
+        if constexpr (DV % 2 == 0) {
 #pragma unroll
-        for (int j = 0; j < DV; ++j) acc[h][j] *= al[h];
+          for (int j = 0; j < DV; j += 2) fmul2_bcast(acc[h][j], acc[h][j + 1], al[h]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < DV; ++j) acc[h][j] *= al[h];
+        }
+      }
       auto pv_token = [&](int t) {
         float v[DV];
         load_v<D>(sv + t * D, lane, v);
