@@ -116,3 +116,16 @@ def test_step_phases():
         assert sc.is_encoding
         sc.memory_barrier()
     assert not sc.is_encoding
+
+
+def test_bridge_constructors_mirror_the_reference():
+    """Bridge classes keep the reference's constructor checks and attributes
+    (metal_paged_attention_v2.py:37-60, metal_paged_attention_fused.py:98-157)."""
+    import pytest as _pytest
+    from vllm_apple_b200.bridge import MetalPagedAttentionFused, MetalPagedAttentionV2
+    with _pytest.raises(ValueError):
+        MetalPagedAttentionV2(2, 14, 80, 16, 0.1)
+    v2 = MetalPagedAttentionV2(2, 14, 64, 16, 0.125)
+    assert v2.queries_per_kv == 7 and v2.max_num_blocks == 256
+    f = MetalPagedAttentionFused(8, 32, 128, 16)
+    assert abs(f.scale - 128 ** -0.5) < 1e-12 and f.is_fused_available and f.queries_per_kv == 4
