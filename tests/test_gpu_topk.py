@@ -94,3 +94,15 @@ def test_topk_rejects():
     assert lib.va_topk(i.data_ptr(), v.data_ptr(), x.data_ptr(), 2, 100, 99, 5, s) == 1
     assert lib.va_topk(i.data_ptr(), v.data_ptr(), x.data_ptr(), 2, 100, 100, 1025, s) == 2
     assert lib.va_topk(i.data_ptr(), v.data_ptr(), x.data_ptr(), 0, 100, 100, 5, s) == 0
+
+
+@pytest.mark.parametrize("T,V,k", [(1, 151936, 50), (8, 131072, 50), (16, 32000, 8),
+                                   (40, 131072, 256), (3, 4100, 20), (64, 262144, 100)])
+@pytest.mark.parametrize("special", [False, True])
+def test_topk_split_rows(T, V, k, special):
+    """Few rows: slices of a row on separate CTAs, then a merge; same results."""
+    from vllm_apple_b200 import _lib
+    lib = _lib.load()
+    if T < 148 and V >= 8192:
+        assert lib.va_topk_workspace_size(T, V, k) > 0  # the split path is taken
+    _check(_logits(T * 11 + V + k, T, V, special), k)

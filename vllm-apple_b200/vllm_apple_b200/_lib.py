@@ -73,6 +73,8 @@ SIGNATURES = {
                         P]),
     "va_silu_mul": (c_int, [P, P, P, I64, P]),
     "va_topk": (c_int, [P, P, P, I64, I64, I64, c_int, P]),
+    "va_topk_workspace_size": (c_size_t, [I64, I64, c_int]),
+    "va_topk_ws": (c_int, [P, P, P, I64, I64, I64, c_int, P, c_size_t, P]),
 }
 
 _lib = None

@@ -373,9 +373,13 @@ class EngineTopK:
                vocab_size: int, k: Optional[int] = None) -> None:
         step_ctx.require_encoding("encode()")
         k = k or self._k
-        _lib.check(_lib.load().va_topk(resolve(indices_out)[0], resolve(values_out)[0],
-                                       resolve(logits)[0], num_tokens, vocab_size, vocab_size, k,
-                                       step_ctx.stream_handle), "va_topk")
+        lib = _lib.load()
+        nbytes = lib.va_topk_workspace_size(num_tokens, vocab_size, k)
+        ws = _ops.workspace(_dev(step_ctx), "topk", nbytes) if nbytes else None
+        _lib.check(lib.va_topk_ws(resolve(indices_out)[0], resolve(values_out)[0],
+                                  resolve(logits)[0], num_tokens, vocab_size, vocab_size, k,
+                                  0 if ws is None else ws.data_ptr(), nbytes,
+                                  step_ctx.stream_handle), "va_topk_ws")
         step_ctx.note_dispatch()
 
     @property
