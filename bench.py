@@ -588,10 +588,16 @@ def run_row(args, rank, local):
         tf = flops / (ms_step * 1e-3) / 1e12
         tpk, tkind = tensor_peak()
         metric, value, unit = "mixed-batch step TFLOP/s (causal prefill FLOPs)", tf, "TFLOP/s"
+        # the step's own lower bound: its HBM bytes at the HBM peak and its FLOPs at the
+        # tensor peak can overlap at best, so the slower of the two bounds the step
+        t_hbm, t_tc = nbytes / (hbm * 1e9) * 1e6, flops / (tpk * 1e12) * 1e6
         roof = {"bound": "tensor", "achieved": round(tf, 2), "peak": tpk, "unit": "TFLOP/s",
                 "frac": round(tf / tpk, 4), "peak_kind": tkind, "traffic": None,
                 "note": "whole step (KV scatter, planner, tiles and decode rows); the decode "
-                        "rows are HBM-bound: GB/s below"}
+                        "rows are HBM-bound: GB/s below",
+                "step_bound_us": {"hbm": round(t_hbm, 1), "tensor": round(t_tc, 1),
+                                  "frac_of_measured": round(max(t_hbm, t_tc) / (ms_step * 1e3),
+                                                            4)}}
     else:
         metric, value, unit = f"{args.row} HBM GB/s (algorithmic bytes)", gbs, "GB/s"
         roof = {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
