@@ -129,3 +129,17 @@ def test_bridge_constructors_mirror_the_reference():
     assert v2.queries_per_kv == 7 and v2.max_num_blocks == 256
     f = MetalPagedAttentionFused(8, 32, 128, 16)
     assert abs(f.scale - 128 ** -0.5) < 1e-12 and f.is_fused_available and f.queries_per_kv == 4
+
+
+def test_bench_row_cpu_legs_run_on_the_host():
+    """The CPU baselines beside each bench row (oracle restatements on a sample) run
+    without a GPU and report positive throughput in the row's unit."""
+    import sys as _sys
+    import os as _os
+    import torch as _torch
+    _sys.path.insert(0, _os.path.dirname(_os.path.dirname(__file__)))
+    import bench
+    for row, unit in (("topk", "GB/s"),):  # (the elementwise cases are 1.6 GB to build)
+        _step, nbytes, flops, launches, cfg, cpu = bench.row_case(row, _torch.device("cpu"))
+        v, u, sample = cpu(0.05)
+        assert v > 0 and u == unit and nbytes > 0 and launches == 1 and "workload" in cfg
