@@ -43,6 +43,34 @@ def _time(fn, iters, warmup) -> float:
     return a.elapsed_time(b) / iters * 1e-3
 
 
+def _time_graph(fn, iters, warmup) -> float:
+    """Device time per call with host launch overhead removed: `iters` calls captured
+    in one CUDA graph, replayed."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fn()  # warm the capture stream (workspaces, side streams)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    g.replay()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(s)
+    g.replay()
+    b.record(s)
+    torch.cuda.synchronize()
+    ops.check_device_errors()
+    return a.elapsed_time(b) / iters * 1e-3
+
+
 def _report(op, sec, nbytes, flops=None, **extra):
     peak = _peak_gbs()
     r = {"op": op, "us": round(sec * 1e6, 2), "bytes": int(nbytes),
@@ -54,16 +82,18 @@ def _report(op, sec, nbytes, flops=None, **extra):
     print(json.dumps(r), flush=True)
 
 
-def run_decode(workload, iters, warmup):
+def run_decode(workload, iters, warmup, graph=False):
     c = make_decode_case(workload, device="cuda", seed=0)
     q, nk, nv = c.q.cuda(), c.new_k.cuda(), c.new_v.cuda()
     bt, sl = c.block_table.cuda(), c.seq_lens.cuda()
     out = torch.empty_like(q)
-    sec = _time(lambda: ops.paged_decode(out, q, c.k_cache, c.v_cache, bt, sl, scale=c.scale,
+    timer = _time_graph if graph else _time
+    sec = timer(lambda: ops.paged_decode(out, q, c.k_cache, c.v_cache, bt, sl, scale=c.scale,
                                          max_seq_len=c.max_seq_len, new_k=nk, new_v=nv),
                 iters, warmup)
     _report("decode", sec, c.algorithmic_bytes(), workload=workload,
-            seq_tokens_per_s=round(c.context_tokens / sec, 1))
+            seq_tokens_per_s=round(c.context_tokens / sec, 1),
+            timing="CUDA graph replay" if graph else "back-to-back launches")
 
 
 def run_mixed(iters, warmup):
@@ -130,10 +160,12 @@ def main():
     ap.add_argument("--workload", default="devstral_b128")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--graph", action="store_true",
+                    help="decode: time a CUDA graph of the calls (no host launch overhead)")
     a = ap.parse_args()
     torch.cuda.set_device(0)
     if a.op in ("decode", "all"):
-        run_decode(a.workload, a.iters, a.warmup)
+        run_decode(a.workload, a.iters, a.warmup, a.graph)
     if a.op in ("mixed", "all"):
         run_mixed(a.iters, a.warmup)
     if a.op in ("rmsnorm", "rope", "silu_mul", "all"):
