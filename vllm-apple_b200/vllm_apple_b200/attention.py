@@ -199,7 +199,9 @@ class MetalAttentionMetadataBuilder(AttentionMetadataBuilder[MetalAttentionMetad
             block_table=c.block_table_tensor, slot_mapping=c.slot_mapping,
             scheduler_metadata=None, causal=c.causal, num_decode_tokens=num_decode_tokens)
         qcpu = getattr(c, "query_start_loc_cpu", None)
-        scpu = getattr(c, "seq_lens_cpu", None)
+        # the cached host copy, when the runner made one (reading vLLM's
+        # ``seq_lens_cpu`` property would force a device sync)
+        scpu = getattr(c, "_seq_lens_cpu", None)
         if qcpu is not None:
             md._query_start_loc_cpu = qcpu.tolist()
         if scpu is not None:
