@@ -1,7 +1,7 @@
 """Generate the golden fixtures of this directory by running the REFERENCE.
 
-Run in a container where the reference tree is mounted (its location is
-VA_REFERENCE_ROOT, with the mount point as the default); the outputs are committed
+Run where the reference's source tree is available (VA_REFERENCE_ROOT, or the
+tree that baseline/_ref was pip-installed from); the outputs are committed
 and the tests read only them, so nothing at test time needs the reference.
 
 What runs (all reference code, unmodified):
@@ -38,41 +38,17 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("VA_REFERENCE_ROOT", "/root/reference")
+sys.path.insert(0, REPO)
+from oracle.reference_loader import reference_source_tree  # noqa: E402
+
+# the reference SOURCE tree: VA_REFERENCE_ROOT, else the tree baseline/_ref was installed from
+REF = reference_source_tree()
 
 
 def load_reference_attention():
     """Import base_attn.py / mps_attn.py of the reference against vLLM 0.22."""
-    import vllm.v1.attention.backend as vb
-    import vllm.v1.attention.backends.utils as vu
-    from vllm.utils.torch_utils import is_quantized_kv_cache
-
-    abstract = types.ModuleType("vllm.attention.backends.abstract")
-    for n in ("AttentionBackend", "AttentionImpl", "AttentionLayer", "AttentionType"):
-        setattr(abstract, n, getattr(vb, n))
-    abstract.is_quantized_kv_cache = is_quantized_kv_cache
-    sys.modules["vllm.attention.backends.abstract"] = abstract
-    for n in ("AttentionMetadataBuilder", "CommonAttentionMetadata"):
-        if not hasattr(vu, n):
-            setattr(vu, n, getattr(vb, n))
-    # package stubs: skip vllm_apple/__init__.py and vllm_apple/v1/__init__.py (they pull in
-    # the Apple worker), but keep the real directories importable
-    for name, sub in (("vllm_apple", "vllm_apple"), ("vllm_apple.v1", "vllm_apple/v1"),
-                      ("vllm_apple.v1.attention", "vllm_apple/v1/attention"),
-                      ("vllm_apple.v1.attention.backends", "vllm_apple/v1/attention/backends")):
-        m = types.ModuleType(name)
-        m.__path__ = [os.path.join(REF, sub)]
-        sys.modules[name] = m
-    mods = {}
-    for stem in ("base_attn", "mps_attn"):
-        path = os.path.join(REF, "vllm_apple/v1/attention/backends", stem + ".py")
-        full = "vllm_apple.v1.attention.backends." + stem
-        spec = importlib.util.spec_from_file_location(full, path)
-        mod = importlib.util.module_from_spec(spec)
-        sys.modules[full] = mod
-        spec.loader.exec_module(mod)
-        mods[stem] = mod
-    return mods["mps_attn"]
+    from oracle.reference_loader import load_reference_attention as _load
+    return _load(REF)
 
 
 def make_meta(mps, T, query_start_loc, seq_lens, block_table, slot_mapping, num_decode):
