@@ -154,9 +154,12 @@ VA_API int va_paged_decode(void *out, const void *q, void *k_cache, void *v_cach
  * array built into the library, VA_DECODE_STATIC_SCRATCH_BYTES per GPU, held by
  * every GPU that loads the library until the process exits.  Shapes whose
  * va_paged_decode_workspace_size exceeds it return VA_ERR_SCRATCH_LIMIT and
- * launch nothing.  The first call on a device (with that device current)
- * looks up the array's device address; make that first call before any stream
- * capture.  All calls share the one array, so calls that overlap on the GPU
+ * launch nothing; a shape va_paged_decode rejects gets the same status here.
+ * The first call on a device (with that device current) looks up the array's
+ * device address; make that first call before any stream capture.  The address
+ * is kept for the life of the process's CUDA context on that device: after a
+ * cudaDeviceReset of that device, do not call this entry point again in the
+ * same process.  All calls share the one array, so calls that overlap on the GPU
  * (different streams, no ordering between them) race; calls ordered on one
  * stream do not.  Allocates nothing.  It has no counterpart in the reference. */
 #define VA_DECODE_STATIC_SCRATCH_BYTES (32u << 20)
@@ -186,7 +189,12 @@ VA_API size_t va_paged_prefill_workspace_size(int64_t num_tokens, int64_t num_se
  * context longer than the block table or a negative block inside the context
  * are skipped (out untouched).  Runs of consecutive tokens of one sequence are
  * processed as tensor-core tiles (tcgen05 UMMA for head_size 64/128); one-token
- * runs go to the split-KV decode kernel.
+ * runs go to the split-KV decode kernel.  With tensor-core tiles, those rows
+ * run on one library-owned side stream per device, forked from and joined back
+ * to `stream` with events (so the call stays stream-ordered and capturable);
+ * calls on one device take that side stream in turn (a mutex), so eager calls
+ * from several threads serialise on it, and a stream capture that includes a
+ * prefill call must not overlap an eager prefill call on the same device.
  * Replaces PagedAttentionOp.encode_prefill
  * (vllm_apple/engine/ops/attention.py:290-367) -- kernel
  * paged_attention_v2_prefill (vllm_apple/metal/kernels/paged_attention_v2.metal:375-478). */

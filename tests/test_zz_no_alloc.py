@@ -8,8 +8,6 @@ as va_paged_decode with a caller workspace, on two calls in a row (the shared
 scratch keeps the previous call's contents), and refuse shapes that need more
 scratch than it has.  This file is collected last on purpose.
 """
-import ctypes
-
 import numpy as np
 import pytest
 import torch
@@ -55,15 +53,34 @@ def test_noalloc_decode_matches_workspace_decode(config, batch):
         assert torch.equal(out, ref_out)
 
 
+def _header_scratch_bytes():
+    """VA_DECODE_STATIC_SCRATCH_BYTES as the public header defines it."""
+    import os
+    import re
+    hdr = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                       "vllm_apple_b200.h")
+    m = re.search(r"#define VA_DECODE_STATIC_SCRATCH_BYTES \((\d+)u << (\d+)\)", open(hdr).read())
+    assert m, "VA_DECODE_STATIC_SCRATCH_BYTES not found in the header"
+    return int(m.group(1)) << int(m.group(2))
+
+
 def test_noalloc_rejects_shapes_beyond_its_scratch():
     from vllm_apple_b200 import _lib
     lib = _lib.load()
+    limit = _header_scratch_bytes()
     # 4096 sequences of up to 65536 tokens need far more split scratch than is built in
     need = lib.va_paged_decode_workspace_size(4096, 32, 8, 128, 16, 65536)
-    assert need > (32 << 20)
-    P = ctypes.c_void_p
-    rc = lib.va_paged_decode_noalloc(P(256), P(256), P(256), P(256), P(256), P(256), None, None,
+    assert need > limit
+    # Every pointer is NULL: whatever order the checks run in, nothing can launch
+    # (va_paged_decode itself rejects NULL buffers before any launch).
+    rc = lib.va_paged_decode_noalloc(None, None, None, None, None, None, None, None,
                                      4096, 32, 8, 128, 16, 4096, 65536, 1 << 20, 0.1,
                                      8 * 16 * 128, 16 * 128, 128, 4096, 128, 4096, 128, 0, 0,
                                      None, None)
     assert rc == _lib.VA_ERR_SCRATCH_LIMIT
+    # a shape va_paged_decode does not support reports that, not the scratch limit
+    rc = lib.va_paged_decode_noalloc(None, None, None, None, None, None, None, None,
+                                     4096, 32, 8, 128, 32, 4096, 65536, 1 << 20, 0.1,
+                                     8 * 32 * 128, 32 * 128, 128, 4096, 128, 4096, 128, 0, 0,
+                                     None, None)
+    assert rc == _lib.VA_ERR_UNSUPPORTED

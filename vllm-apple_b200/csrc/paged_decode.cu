@@ -24,13 +24,14 @@
 //     to the cache; no other CTA reads that slot.
 #include <math.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
 
 namespace {
 
-// Tuning knobs (defaults are the measured best on B200; see profiles/).
+// Tuning knobs (defaults are the measured best on B200).
 #ifndef VA_DECODE_STAGES
 #define VA_DECODE_STAGES 2
 #endif
@@ -673,15 +674,17 @@ WsLayout ws_layout(int64_t num_seqs, int Hq, int Hkv, int D, const Plan &p) {
 template <int D, int GC, int BS>
 int launch_t(const DecodeArgs &a, dim3 grid, cudaStream_t st) {
   using C = Cfg<D, GC, BS>;
-  static int configured[64] = {0};
+  // per-device opt-in to the kernel's dynamic shared memory (setting it twice from
+  // two threads is harmless; the flag only saves the call)
+  static std::atomic<int> configured[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !configured[dev]) {
+  if (dev >= 0 && dev < 64 && !configured[dev].load(std::memory_order_acquire)) {
     if (cudaFuncSetAttribute(paged_decode_kernel<D, GC, BS>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)C::kSmem) != cudaSuccess)
       return VA_ERR_LAUNCH;
-    configured[dev] = 1;
+    configured[dev].store(1, std::memory_order_release);
   }
   paged_decode_kernel<D, GC, BS><<<grid, kNW * 32, C::kSmem, st>>>(a);
   if (grid.x > 1) {
@@ -893,6 +896,14 @@ extern "C" int va_paged_decode_noalloc(void *out, const void *q, void *k_cache, 
                                        int64_t q_s_token, int64_t q_s_head, int64_t o_s_token,
                                        int64_t o_s_head, int64_t new_s_token,
                                        int64_t new_s_head, int32_t *err_flag, void *stream) {
+  // the shape checks of va_paged_decode come first, so a shape it would reject
+  // reports the same status here, whatever its scratch need
+  if (num_seqs < 0 || max_seq_len < 0 || num_blocks < 0 || max_blocks_per_seq < 0 ||
+      num_kv_heads <= 0 || num_query_heads <= 0 || num_query_heads % num_kv_heads)
+    return VA_ERR_INVALID_ARG;
+  if (num_seqs > 65535 || block_size != 16 ||
+      (head_size != 32 && head_size != 64 && head_size != 96 && head_size != 128))
+    return VA_ERR_UNSUPPORTED;
   const size_t need = va_paged_decode_workspace_size(num_seqs, num_query_heads, num_kv_heads,
                                                      head_size, block_size, max_seq_len);
   if (need > (size_t)VA_DECODE_STATIC_SCRATCH_BYTES) return VA_ERR_SCRATCH_LIMIT;

@@ -112,7 +112,7 @@ class PagedAttentionOp:
         nbytes = lib.va_paged_decode_workspace_size(num_seqs, self.num_query_heads,
                                                     self.num_kv_heads, self.head_size,
                                                     self.block_size, max_seq_len)
-        ws = _ops.workspace(dev, "decode", nbytes) if nbytes else None
+        ws = _ops.workspace(dev, "decode", nbytes, step_ctx.stream) if nbytes else None
         _lib.check(lib.va_paged_decode(
             out, q, kc, vc, bt, sl, nk, nv, num_seqs, self.num_query_heads, self.num_kv_heads,
             self.head_size, self.block_size, max_blocks, max_seq_len, self._num_blocks(kb),
@@ -139,7 +139,7 @@ class PagedAttentionOp:
         nbytes = lib.va_paged_prefill_workspace_size(num_tokens, num_seqs, self.num_query_heads,
                                                      self.num_kv_heads, self.head_size,
                                                      self.block_size, max_blocks_per_seq)
-        ws = _ops.workspace(dev, "prefill", nbytes)
+        ws = _ops.workspace(dev, "prefill", nbytes, step_ctx.stream)
         _lib.check(lib.va_paged_prefill(
             out, q, kc, vc, resolve(block_table_buffer)[0], resolve(token_to_seq_buffer)[0],
             resolve(positions_buffer)[0], num_tokens, num_seqs, self.num_query_heads,
@@ -375,7 +375,7 @@ class EngineTopK:
         k = k or self._k
         lib = _lib.load()
         nbytes = lib.va_topk_workspace_size(num_tokens, vocab_size, k)
-        ws = _ops.workspace(_dev(step_ctx), "topk", nbytes) if nbytes else None
+        ws = _ops.workspace(_dev(step_ctx), "topk", nbytes, step_ctx.stream) if nbytes else None
         _lib.check(lib.va_topk_ws(resolve(indices_out)[0], resolve(values_out)[0],
                                   resolve(logits)[0], num_tokens, vocab_size, vocab_size, k,
                                   0 if ws is None else ws.data_ptr(), nbytes,

@@ -22,7 +22,7 @@ from . import _lib
 
 _state_lock = threading.Lock()
 _err_flags: dict[int, torch.Tensor] = {}
-_workspaces: dict[tuple[int, str], torch.Tensor] = {}
+_workspaces: dict[tuple[int, str, int], torch.Tensor] = {}
 
 
 # ---------------------------------------------------------------------------
@@ -57,17 +57,27 @@ def check_device_errors(device: int | None = None, raise_on_error: bool = True) 
     return bits
 
 
-def workspace(device: int, kind: str, nbytes: int) -> torch.Tensor:
-    """A device scratch buffer of at least ``nbytes`` (grown on demand, never
-    shrunk).  Calls on one device share it; stream order keeps them apart."""
+def workspace(device: int, kind: str, nbytes: int,
+              stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """A device scratch buffer of at least ``nbytes`` for calls enqueued on
+    ``stream`` (default: the device's current stream), grown on demand.
+
+    One buffer per (device, kind, stream): calls on one stream are ordered, so
+    they may share it; calls on different streams get different buffers and
+    cannot race.  A grown buffer is allocated while ``stream`` is current, so the
+    caching allocator reuses the old one only behind the work already queued
+    on that stream."""
+    st = torch.cuda.current_stream(device) if stream is None else stream
+    key = (device, kind, st.cuda_stream)
     with _state_lock:
-        ws = _workspaces.get((device, kind))
+        ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:
             size = max(nbytes, 1 << 16)
             if ws is not None:
                 size = max(size, 2 * ws.numel())
-            ws = torch.empty(size, dtype=torch.uint8, device=f"cuda:{device}")
-            _workspaces[(device, kind)] = ws
+            with torch.cuda.stream(st):
+                ws = torch.empty(size, dtype=torch.uint8, device=f"cuda:{device}")
+            _workspaces[key] = ws
         return ws
 
 

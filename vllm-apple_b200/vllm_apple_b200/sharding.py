@@ -53,19 +53,44 @@ class ShardPlan:
         return own
 
 
+class OutputGather:
+    """All-gather of the per-rank decode outputs back into batch order.
+
+    Each rank contributes its ``[len(shard), ...]`` rows padded to the widest
+    shard; one ``all_gather_into_tensor`` (NCCL over NVLink) fills a
+    ``[world * width, ...]`` buffer, and one device gather with a permutation
+    built once puts the rows in the original sequence order.  Buffers are
+    allocated once, so repeated calls launch exactly one collective and two
+    small copy kernels."""
+
+    def __init__(self, plan: ShardPlan, row_shape, dtype, device, group=None):
+        self.plan, self.group = plan, group
+        self.width = max(len(s) for s in plan.shards)
+        self.pad = torch.zeros((self.width,) + tuple(row_shape), dtype=dtype, device=device)
+        self.buf = torch.empty((plan.world * self.width,) + tuple(row_shape), dtype=dtype,
+                               device=device)
+        src = torch.empty(len(plan.lengths), dtype=torch.int64)
+        for r, s in enumerate(plan.shards):
+            for j, i in enumerate(s):
+                src[i] = r * self.width + j
+        self.src = src.to(device)
+        self.full = torch.empty((len(plan.lengths),) + tuple(row_shape), dtype=dtype,
+                                device=device)
+
+    @property
+    def bytes_per_rank(self) -> int:
+        return self.pad.numel() * self.pad.element_size()
+
+    def __call__(self, local_out: torch.Tensor) -> torch.Tensor:
+        import torch.distributed as dist
+        self.pad[:local_out.shape[0]].copy_(local_out)
+        dist.all_gather_into_tensor(self.buf, self.pad, group=self.group)
+        torch.index_select(self.buf, 0, self.src, out=self.full)
+        return self.full
+
+
 def gather_outputs(local_out: torch.Tensor, plan: ShardPlan, rank: int, group=None) -> torch.Tensor:
     """All-gather each rank's [len(shard), ...] outputs and return the full
     batch [B, ...] in the original sequence order (on every rank)."""
-    import torch.distributed as dist
-    width = max(len(s) for s in plan.shards)
-    pad = torch.zeros((width,) + tuple(local_out.shape[1:]), dtype=local_out.dtype,
-                      device=local_out.device)
-    pad[:local_out.shape[0]] = local_out
-    bufs = [torch.empty_like(pad) for _ in range(plan.world)]
-    dist.all_gather(bufs, pad, group=group)
-    full = torch.empty((len(plan.lengths),) + tuple(local_out.shape[1:]), dtype=local_out.dtype,
-                       device=local_out.device)
-    for r, s in enumerate(plan.shards):
-        if s:
-            full[torch.as_tensor(s, device=full.device)] = bufs[r][:len(s)]
-    return full
+    g = OutputGather(plan, local_out.shape[1:], local_out.dtype, local_out.device, group)
+    return g(local_out).clone()
