@@ -137,3 +137,52 @@ def test_prefill_bad_block_is_flagged_and_skipped():
     assert good.any() and (~good).any()
     assert max_abs(np16(out)[good], o[good]) <= ATOL
     assert torch.all(out.cpu()[torch.from_numpy(~good)] == 7.0)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("layout", ["hnd", "nhd"])
+def test_prefill_long_context_key_range_parts(D, layout):
+    """Few tiles over long prior contexts: each tile's keys are cut into ranges
+    processed by different CTAs (partial O, m, l merged by the part that finishes
+    last, in part order).  Results as the oracle, and repeated calls agree bit for
+    bit (the merge order does not depend on which part finishes last)."""
+    from vllm_apple_b200.workloads import make_mixed_case
+    Hq, Hkv = (32, 8) if D == 128 else (14, 2)
+    c = make_mixed_case(D=D, Hq=Hq, Hkv=Hkv, layout=layout, num_chunks=2, chunk=64,
+                        prior=(3000, 6000), num_decode=2, decode_len=(100, 3000), seed=D + 1)
+    out, _, _, bad = _run(c)
+    assert bad == 0
+    o, _, _ = _oracle(c)
+    assert max_abs(np16(out), o) <= ATOL
+    out2, _, _, _ = _run(c)
+    assert torch.equal(out, out2)
+
+
+@pytest.mark.parametrize("where", ["early", "late"])
+def test_prefill_bad_block_in_a_cut_tile(where):
+    """A bad block id inside one key range of a tile that is cut into parts: rows
+    whose context reaches it stay unwritten (all of them when it lies in an early
+    range), the others are exact, and the flag is raised."""
+    from vllm_apple_b200 import ops
+    from vllm_apple_b200.workloads import make_mixed_case
+    c = make_mixed_case(num_chunks=1, chunk=64, prior=(4000, 4000), num_decode=0, seed=11)
+    bs = c.bs
+    page = 1000 // bs if where == "early" else (4000 + 30) // bs
+    bt = c.block_table.clone()
+    bt[0, page] = c.num_blocks + 3
+    dk, dv = c.k_cache.cuda(), c.v_cache.cuda()
+    ops.kv_write_slots(dk, dv, c.k.cuda(), c.v.cuda(), c.slot_mapping.cuda(), c.layout)
+    q = c.q.cuda()
+    out = torch.full_like(q, 7.0)
+    ops.paged_prefill(out, q, dk, dv, bt.cuda(), c.token_to_seq.cuda(), c.positions.cuda(),
+                      scale=c.scale, layout=c.layout)
+    torch.cuda.synchronize()
+    assert ops.check_device_errors(raise_on_error=False) & 2
+    o, _, _ = _oracle(c)
+    good = c.positions.numpy() < page * bs
+    if where == "early":
+        assert not good.any()
+    else:
+        assert good.any() and (~good).any()
+        assert max_abs(np16(out)[good], o[good]) <= ATOL
+    assert torch.all(out.cpu()[torch.from_numpy(~good)] == 7.0)

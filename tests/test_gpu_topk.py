@@ -106,3 +106,33 @@ def test_topk_split_rows(T, V, k, special):
     if T < 148 and V >= 8192:
         assert lib.va_topk_workspace_size(T, V, k) > 0  # the split path is taken
     _check(_logits(T * 11 + V + k, T, V, special), k)
+
+
+@pytest.mark.parametrize("T,V,k", [(32, 32000, 50), (4, 151936, 256), (1024, 131072, 50)])
+def test_topk_matches_torch_topk_on_distinct_values(T, V, k):
+    """Independent of the oracle: on rows whose values are all distinct (a random
+    permutation of distinct fp16 values), the selection is unique, so indices and
+    values must equal torch.topk's (sorted, largest first)."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(T + V + k)
+    # 2^15 - 2048 distinct finite fp16 values, each row a random draw without repeats
+    pool = torch.arange(-30000, 30000, dtype=torch.int32)
+    vals = pool.to(torch.int16).view(torch.float16)
+    vals = vals[torch.isfinite(vals)]
+    vals = torch.unique(vals.float()).half()
+    assert vals.numel() >= min(V, 28000)
+    rows = []
+    for _ in range(T):
+        pick = torch.randperm(vals.numel(), generator=g)[:min(V, vals.numel())]
+        r = vals[pick]
+        if V > r.numel():  # pad with -inf (never selected)
+            r = torch.cat([r, torch.full((V - r.numel(),), float("-inf"), dtype=torch.float16)])
+        rows.append(r)
+    x = torch.stack(rows)
+    dx = x.cuda()
+    idx = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    val = torch.empty(T, k, dtype=torch.float16, device="cuda")
+    ops.topk(idx, val, dx, k)
+    tv, ti = torch.topk(dx.float(), k, dim=1, largest=True, sorted=True)
+    assert torch.equal(idx.long(), ti)
+    assert torch.equal(val.float(), tv)

@@ -51,12 +51,48 @@ constexpr int kThreads = 128;
 // ---------------------------------------------------------------------------
 constexpr int kOrderBuckets = 2048;
 
+// Key-range parts of the tensor-core items (filled when `units` is given).
+struct UnitPlan {
+  int4 *units;        // [max_units] {tile, part | parts << 16, planned chunks, slot base}
+  int32_t *tickets;   // [max_tiles * ny] arrival counters, zeroed here
+  int ny;             // items per unit (kv heads x q-head groups)
+  int nsm;            // SMs of the device
+  int slot_cap;       // partial-result slots available
+  int max_units;
+};
+
+// Exclusive block-wide scan (1024 threads) of v; returns the prefix, *total the sum.
+VA_DEVINL int block_excl_scan(int v, int *warp_buf, int *total) {
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  int x = v;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += n;
+  }
+  if (lane == 31) warp_buf[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    int w = warp_buf[lane];
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += n;
+    }
+    warp_buf[lane] = w;
+  }
+  __syncthreads();
+  const int excl = x - v + (wid > 0 ? warp_buf[wid - 1] : 0);
+  *total = warp_buf[31];
+  __syncthreads();
+  return excl;
+}
+
 __global__ void __launch_bounds__(1024) plan_tiles_kernel(const int32_t *token_to_seq,
                                                           const int32_t *positions,
                                                           int64_t T, int TQ, int2 *tiles,
                                                           int32_t *tiles_n, int64_t max_tiles,
                                                           int32_t *singles, int32_t *singles_n,
-                                                          int32_t *order, int32_t *err) {
+                                                          int32_t *order, int32_t *err,
+                                                          UnitPlan up) {
   __shared__ int warp_buf[32];
   __shared__ int carry_max, carry_sum, n_single;
   __shared__ int bucket[kOrderBuckets];
@@ -171,6 +207,82 @@ __global__ void __launch_bounds__(1024) plan_tiles_kernel(const int32_t *token_t
   }
   __syncthreads();
   for (int i = tid; i < n; i += 1024) order[atomicAdd(&bucket[bucket_of(i)], 1)] = i;
+  if (!up.units) return;
+  __syncthreads();
+  // ---- key-range parts: long tiles are cut into parts of about KP chunks of 64
+  // keys, so the persistent grid's last items are short.  KP is half the
+  // per-SM share of all the work (>= 16 chunks); the longest tiles are cut first,
+  // as long as partial-result slots last.  Units follow the tile order (longest
+  // first), the parts of a tile consecutively. ----
+  auto chunks_of = [&](int i) {
+    const int2 t = tiles[i];
+    const int p = positions[t.x + t.y - 1];
+    return (p < 0 || (singles && t.y == 1)) ? 0 : (p + 64) / 64;
+  };
+  __shared__ unsigned long long work_sum;
+  __shared__ int carry_slot, carry_unit;
+  if (tid == 0) { work_sum = 0ull; carry_slot = 0; carry_unit = 0; }
+  __syncthreads();
+  __shared__ int busy_tiles;
+  if (tid == 0) busy_tiles = 0;
+  __syncthreads();
+  unsigned long long wloc = 0;
+  int bloc = 0;
+  for (int i = tid; i < n; i += 1024) {
+    const int c = chunks_of(i);
+    wloc += (unsigned long long)c;
+    bloc += c > 0;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    wloc += __shfl_xor_sync(0xffffffffu, wloc, o);
+    bloc += __shfl_xor_sync(0xffffffffu, bloc, o);
+  }
+  if (lane == 0 && wloc) atomicAdd(&work_sum, wloc);
+  if (lane == 0 && bloc) atomicAdd(&busy_tiles, bloc);
+  __syncthreads();
+  // Cutting costs each part a pipeline fill, a partial write and (last part) a
+  // merge; measured on B200 it pays only when there are fewer items than SMs
+  // (config-4 shapes: 120 items at head_size 64 gained 11 %, 256 at head_size 128
+  // lost 15 %), so tiles are cut only then.
+  const bool cut = (long long)busy_tiles * up.ny < up.nsm;
+  if (!cut) {  // one unit per tile, in the tile order
+    for (int i = tid; i < n; i += 1024) {
+      const int tile = order[i];
+      up.units[i] = make_int4(tile, 1 << 16, chunks_of(tile), -1);
+    }
+    if (tid == 0) tiles_n[3] = n;
+    return;
+  }
+  for (int i = tid; i < n * up.ny; i += 1024) up.tickets[i] = 0;
+  const unsigned long long per_sm = work_sum * (unsigned long long)up.ny / (2ull * up.nsm);
+  const int KP = (int)max(16ull, min(per_sm, 1ull << 20));
+  for (int base = 0; base < n; base += 1024) {
+    const int i = base + tid;
+    const bool in = i < n;
+    const int tile = in ? order[i] : 0;
+    const int nch = in ? chunks_of(tile) : 0;
+    int np = nch > KP ? (nch + KP - 1) / KP : 1;
+    int tot;
+    const int need = (in && np > 1) ? np * up.ny : 0;
+    const int sbase = block_excl_scan(need, warp_buf, &tot) + carry_slot;
+    int slot = -1;
+    if (np > 1) {
+      if (sbase + need <= up.slot_cap) slot = sbase;
+      else np = 1;
+    }
+    const int ubase = block_excl_scan(in ? np : 0, warp_buf, &tot) + carry_unit;
+    if (in)
+      for (int p = 0; p < np; ++p)
+        if (ubase + p < up.max_units)
+          up.units[ubase + p] = make_int4(tile, p | (np << 16), nch, slot);
+    __syncthreads();
+    if (tid == 1023) {
+      carry_slot = sbase + need;
+      carry_unit = ubase + (in ? np : 0);
+    }
+    __syncthreads();
+  }
+  if (tid == 0) tiles_n[3] = min(carry_unit, up.max_units);
 }
 
 // ---------------------------------------------------------------------------
@@ -601,11 +713,15 @@ size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // Workspace layout of one prefill call: [counters | tiles | one-token rows | decode partials].
 struct PrefillPlan {
-  int TQ, gc;
+  int TQ, gc, ny, slot_cap, max_units;
   bool tc, route;
   int64_t mt, rows_bound;
-  size_t o_tiles, o_singles, o_order, o_dec, dec_bytes, total;
+  size_t o_tiles, o_singles, o_order, o_units, o_tickets, o_part_o, o_part_ml, o_part_bad,
+      o_dec, dec_bytes, total;
 };
+
+// Bytes of partial results the tensor-core kernel may use for key-range parts.
+constexpr size_t kPartBudget = size_t(64) << 20;
 
 // `tc_layout` >= 0 when the tcgen05/TMA tile kernel can take this cache.  Buffer
 // sizes use the smaller tile (more tiles) so they do not depend on the choice.
@@ -623,7 +739,32 @@ PrefillPlan prefill_plan(int64_t T, int64_t S, int Hq, int Hkv, int D, int bs, i
   p.o_tiles = 256;
   p.o_singles = p.o_tiles + align256((size_t)bound * sizeof(int2));
   p.o_order = p.o_singles + align256((size_t)bound * sizeof(int32_t));
-  p.o_dec = p.o_order + align256((size_t)bound * sizeof(int32_t));
+  size_t at = p.o_order + align256((size_t)bound * sizeof(int32_t));
+  if (p.tc) {
+    // key-range parts of long tiles: unit list, per-(tile, item) tickets, and
+    // partial (O, m, l) slots -- at most kPartBudget, and no more than every tile
+    // cut into parts of 16 chunks could use
+    p.ny = Hkv * ((Hq / Hkv) / p.gc);
+    const size_t slot_bytes = (size_t)tc::kTiles * tc::kRows * ((size_t)D + 2) * 4 + 4;
+    const int64_t max_nch = (maxb * bs + tc::kKeys - 1) / tc::kKeys;
+    const int64_t maxp = (max_nch + 15) / 16;
+    int64_t cap = (int64_t)(kPartBudget / slot_bytes);
+    const int64_t want = maxp > 1 ? p.mt * p.ny * maxp : 0;
+    cap = cap < want ? cap : want;
+    p.slot_cap = (int)(cap < (1 << 24) ? cap : (1 << 24));
+    p.max_units = (int)(p.mt + p.slot_cap);
+    p.o_units = at;
+    at += align256((size_t)p.max_units * sizeof(int4));
+    p.o_tickets = at;
+    at += align256((size_t)p.mt * p.ny * sizeof(int32_t));
+    p.o_part_o = at;
+    at += align256((size_t)p.slot_cap * tc::kTiles * tc::kRows * D * 4);
+    p.o_part_ml = at;
+    at += align256((size_t)p.slot_cap * tc::kTiles * tc::kRows * 8);
+    p.o_part_bad = at;
+    at += align256((size_t)p.slot_cap * 4);
+  }
+  p.o_dec = at;
   p.dec_bytes = p.route ? va_internal::decode_rows_workspace(bound, Hq, Hkv, D, bs, maxb) : 0;
   p.total = p.o_dec + p.dec_bytes;
   return p;
@@ -690,10 +831,19 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
   int32_t *singles = reinterpret_cast<int32_t *>(ws + pl.o_singles);
   auto st = static_cast<cudaStream_t>(stream);
   int32_t *order = reinterpret_cast<int32_t *>(ws + pl.o_order);
+  UnitPlan up{};
+  if (use_tc) {
+    up.units = reinterpret_cast<int4 *>(ws + pl.o_units);
+    up.tickets = reinterpret_cast<int32_t *>(ws + pl.o_tickets);
+    up.ny = pl.ny;
+    up.nsm = va_host::sm_count();
+    up.slot_cap = pl.slot_cap;
+    up.max_units = pl.max_units;
+  }
   plan_tiles_kernel<<<1, 1024, 0, st>>>(token_to_seq, positions, num_tokens, TQ, tiles, tiles_n,
                                         mt, pl.route ? singles : nullptr,
                                         pl.route ? singles_n : nullptr,
-                                        use_tc ? order : nullptr, err_flag);
+                                        use_tc ? order : nullptr, err_flag, up);
   if (va_host::launch_status() != VA_OK) return VA_ERR_LAUNCH;
   auto launch_rows = [&](cudaStream_t rs) {
     return va_internal::decode_rows(
@@ -763,7 +913,11 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
   if (use_tc) {
     tc::Args t{};
     t.out = a.out; t.q = a.q; t.kc = a.kc; t.vc = a.vc; t.bt = a.bt; t.tok_seq = a.tok_seq;
-    t.pos = a.pos; t.tiles = a.tiles; t.order = order; t.tiles_n = a.tiles_n; t.err = a.err;
+    t.pos = a.pos; t.tiles = a.tiles; t.err = a.err;
+    t.units = up.units; t.units_n = tiles_n + 3; t.tickets = up.tickets;
+    t.part_o = reinterpret_cast<float *>(ws + pl.o_part_o);
+    t.part_ml = reinterpret_cast<float2 *>(ws + pl.o_part_ml);
+    t.part_bad = reinterpret_cast<int32_t *>(ws + pl.o_part_bad);
     t.work = tiles_n + 2;
     t.num_seqs = a.num_seqs; t.max_blocks = a.max_blocks; t.num_blocks = a.num_blocks;
     t.Hq = a.Hq; t.Hkv = a.Hkv; t.G = a.G; t.hgroups = a.hgroups; t.TQ = a.TQ / tc::kTiles;
@@ -778,8 +932,8 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
         !encode_page_map(&mv, v_cache, layout, num_blocks, num_kv_heads, block_size, head_size))
       return VA_ERR_LAUNCH;
     // persistent: one CTA per SM (shared memory and TMEM allow no more), items
-    // taken in the planner's longest-first order
-    const int64_t nitems = mt * (int64_t)grid.y;
+    // taken in the planner's longest-first order (bounded by its unit capacity)
+    const int64_t nitems = (int64_t)pl.max_units * grid.y;
     if (nitems > INT32_MAX) return VA_ERR_UNSUPPORTED;
     const int64_t nsm = va_host::sm_count();
     const dim3 grid1((unsigned)(nitems < nsm ? nitems : nsm));

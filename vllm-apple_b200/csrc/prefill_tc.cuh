@@ -232,8 +232,12 @@ struct Args {
   const __half *q, *kc, *vc;
   const int32_t *bt, *tok_seq, *pos;
   const int2 *tiles;
-  const int32_t *order;  // tile indices, longest context first
-  const int32_t *tiles_n;
+  const int4 *units;      // {tile, part | parts << 16, planned chunks, slot base}, longest first
+  const int32_t *units_n;
+  int32_t *tickets;       // [tile * ny + yb] parts finished (zeroed by the planner)
+  float *part_o;          // [slot][tile h][D][kRows] un-normalised O of a key-range part
+  float2 *part_ml;        // [slot][tile h][kRows] (m, l) of that part
+  int32_t *part_bad;      // [slot] first context position behind a bad block (INT_MAX: none)
   int32_t *work;  // item counter (zeroed by the planner)
   int32_t *err;
   int64_t num_seqs, max_blocks, num_blocks;
@@ -257,6 +261,8 @@ struct Smem {
 
 // Named barrier over the softmax and MMA warps (the producer warp runs free).
 VA_DEVINL void math_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kMath) : "memory"); }
+// The softmax warpgroups (both tiles), for the key-range part epilogue.
+VA_DEVINL void softmax_sync() { asm volatile("bar.sync 3, %0;" ::"n"(kSoftmax) : "memory"); }
 // Every warp of the CTA, met from different places in the role code.
 VA_DEVINL void all_sync() { asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory"); }
 
@@ -276,12 +282,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *bar_done = bar_pv + kTiles;      // [kTiles] every MMA of the tile retired
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar_done + kTiles);
   int *s_pos = reinterpret_cast<int *>(smem + S::oPos);  // [kTiles][kRows]
-  __shared__ int s_ctx[kTiles], s_bad_from, s_dead, s_item[2];
+  __shared__ int s_ctx[kTiles], s_bad_from, s_dead, s_item[2], s_last;
 
   const int ny = a.Hkv * a.hgroups;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int BS = a.bs, TQ = a.TQ;
-  const int nitems = *a.tiles_n * ny;
+  const int nitems = *a.units_n * ny;
   if ((int)blockIdx.x >= nitems) return;
   if (tid == 0) s_dead = 0;
   if (warp == kMmaWarp) tmem_alloc(tmem_slot, kTmemCols);
@@ -310,7 +316,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int it = s_item[iter & 1];
     if (it >= nitems || dead()) break;  // uniform
     const int item = it / ny, yb = it - item * ny;
-    const int tile = a.order[item];
+    const int4 unit = a.units[item];
+    const int tile = unit.x, kpart = unit.y & 0xFFFF, nparts = unit.y >> 16;
     const int2 td = a.tiles[tile];
     const int t0 = td.x, nq = td.y;
     if (nq == 1 && a.skip_singles) continue;  // handled by the split-KV decode kernel
@@ -360,8 +367,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     fence_after_sync();
     const int ctx = max(s_ctx[0], s_ctx[1]);
-    if (ctx == 0) continue;  // nothing to attend (all tokens skipped)
-    const int nch = (ctx + kKeys - 1) / kKeys;
+    if (ctx == 0) continue;  // nothing to attend (all tokens skipped): in every part
+    const int nch_all = (ctx + kKeys - 1) / kKeys;
+    // this unit's key range: chunks [cb, cb + nch) of the context (all of it when
+    // the tile is not cut into parts)
+    const int cb = nparts > 1 ? kpart * unit.z / nparts : 0;
+    const int ce = nparts > 1 ? min((kpart + 1) * unit.z / nparts, nch_all) : nch_all;
+    const int nch = ce > cb ? ce - cb : 0;
     const int32_t *bt_row = a.bt + (int64_t)seq * a.max_blocks;
 
     if (warp == kProducerWarp) {
@@ -374,11 +386,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int page = g * 32 + lane;
         return page < pages ? __ldg(bt_row + page) : -1;
       };
-      int gi = 0;
-      int32_t g_cur = load_group(0), g_next = load_group(1);
+      int gi = (cb * npc) >> 5;
+      int32_t g_cur = load_group(gi), g_next = load_group(gi + 1);
 #pragma unroll 1
-      for (int c = 0; c < nch; ++c) {
-        const int buf = c % kStages;
+      for (int i = 0; i < nch; ++i) {  // i: local chunk index, c: chunk of the context
+        const int c = cb + i;
+        const int buf = i % kStages;
         const int first = c * npc;
         if ((first >> 5) != gi) {
           gi = first >> 5;
@@ -386,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           g_next = load_group(gi + 1);
         }
         const int32_t gid = __shfl_sync(0xffffffffu, g_cur, (first & 31) + (lane & (npc - 1)));
-        if (c >= kStages) wait_bar(&bar_empty[buf], (uint32_t)(((c / kStages) - 1) & 1));
+        if (i >= kStages) wait_bar(&bar_empty[buf], (uint32_t)(((i / kStages) - 1) & 1));
         // page ids of this chunk (lane p holds page p)
         int32_t id = -1;
         const int page = first + lane;
@@ -482,7 +495,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (warp > kProducerWarp) {
         // =================== MMA issue for tile h (lane 0) ===================
         const int h = warp - kMmaWarp;
-        const int nj = (s_ctx[h] + kKeys - 1) / kKeys;
+        // local chunks of this unit that hold keys of tile h
+        const int nj = min(max((s_ctx[h] + kKeys - 1) / kKeys - cb, 0), nch);
         const uint32_t sQ = va::smem_addr(smem + S::oQ) + h * S::kQ;
         const uint32_t sK = va::smem_addr(smem + S::oK);
         const uint32_t sV = va::smem_addr(smem + S::oV);
@@ -563,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tO = tmem + 4 * kKeys + h * D + lane_base;
         const int tk = row / GC;
         const int my_pos = (tk < TQ) ? s_pos[h * kRows + tk] : -1;
-        const int nj = (s_ctx[h] + kKeys - 1) / kKeys;
+        const int nj = min(max((s_ctx[h] + kKeys - 1) / kKeys - cb, 0), nch);
         // m: the max the probabilities are taken against.  It only moves when the row
         // max exceeds it by more than 2^8 (P stays <= 256, exact enough in fp16, and
         // O / l at the end cancels it), so O is rescaled in TMEM rarely.
@@ -588,7 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float alpha;
           {
             // raw scores: the scale (> 0) is applied in the exponent's FMA
-            const int vis = my_pos - j * kKeys;  // keys 0..vis of this chunk are visible
+            const int vis = my_pos - (cb + j) * kKeys;  // keys 0..vis of this chunk are visible
             if (vis < kKeys - 1) {
 #pragma unroll
               for (int c = 0; c < kKeys; ++c) p[c] = c <= vis ? p[c] : -INFINITY;
@@ -670,26 +684,92 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int bad_from = s_bad_from;
         if (bad_from != INT_MAX && tid == 0) va::raise_flag(a.err, VA_FLAG_BAD_BLOCK);
         const int ti = h * TQ + tk;
-        const bool write = ok && nj > 0 && my_pos >= 0 && my_pos < bad_from && tk < TQ && ti < nq &&
-                           row < TQ * GC;
-        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const bool row_ok = my_pos >= 0 && tk < TQ && ti < nq && row < TQ * GC;
         const int g = row - tk * GC;
         __half *orow = a.out + (int64_t)(t0 + ti) * a.o_s_token + (int64_t)(head0 + g) * a.o_s_head;
-        if (ok && nj > 0) {
-#pragma unroll 1
-          for (int c = 0; c < D; c += 32) {
-            uint32_t o[32];
-            tmem_ld32(tO + c, o);
-            tmem_wait_ld();
-            if (write) {
+        auto store32 = [&](int c, const float (&v)[32], float inv) {
 #pragma unroll
-              for (int i = 0; i < 32; i += 8) {
-                uint4 w;
-                w.x = va::pack_h2(__uint_as_float(o[i + 0]) * inv, __uint_as_float(o[i + 1]) * inv);
-                w.y = va::pack_h2(__uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
-                w.z = va::pack_h2(__uint_as_float(o[i + 4]) * inv, __uint_as_float(o[i + 5]) * inv);
-                w.w = va::pack_h2(__uint_as_float(o[i + 6]) * inv, __uint_as_float(o[i + 7]) * inv);
-                *reinterpret_cast<uint4 *>(orow + c + i) = w;
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w;
+            w.x = va::pack_h2(v[i + 0] * inv, v[i + 1] * inv);
+            w.y = va::pack_h2(v[i + 2] * inv, v[i + 3] * inv);
+            w.z = va::pack_h2(v[i + 4] * inv, v[i + 5] * inv);
+            w.w = va::pack_h2(v[i + 6] * inv, v[i + 7] * inv);
+            *reinterpret_cast<uint4 *>(orow + c + i) = w;
+          }
+        };
+        if (nparts == 1) {
+          const bool write = ok && nj > 0 && row_ok && my_pos < bad_from;
+          const float inv = l > 0.f ? 1.f / l : 0.f;
+          if (ok && nj > 0) {
+#pragma unroll 1
+            for (int c = 0; c < D; c += 32) {
+              uint32_t o[32];
+              tmem_ld32(tO + c, o);
+              tmem_wait_ld();
+              if (write) {
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]);
+                store32(c, v, inv);
+              }
+            }
+          }
+        } else {
+          // A key-range part: publish (O, m, l) of every row, take a ticket; the
+          // part that finishes last merges all parts in part order and writes
+          // the rows (no CTA waits for another).
+          const int slot0 = unit.w + yb * nparts;
+          const size_t sp = (size_t)(slot0 + kpart) * kTiles + h;
+          float *po = a.part_o + sp * D * kRows + row;  // column-major: coalesced per d
+          const bool have = ok && nj > 0;
+          if (have) {
+#pragma unroll 1
+            for (int c = 0; c < D; c += 32) {
+              uint32_t o[32];
+              tmem_ld32(tO + c, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) __stcg(po + (size_t)(c + i) * kRows, __uint_as_float(o[i]));
+            }
+          }
+          __stcg(a.part_ml + sp * kRows + row, have ? make_float2(m, l) : make_float2(-INFINITY, 0.f));
+          if (tid == 0) __stcg(a.part_bad + slot0 + kpart, bad_from);
+          __threadfence();
+          softmax_sync();
+          if (tid == 0) s_last = atomicAdd(a.tickets + tile * ny + yb, 1) == nparts - 1;
+          softmax_sync();
+          if (s_last) {
+            __threadfence();
+            int bad = INT_MAX;
+            float M = -INFINITY;
+            for (int p = 0; p < nparts; ++p) {
+              bad = min(bad, __ldcg(a.part_bad + slot0 + p));
+              M = fmaxf(M, __ldcg(a.part_ml + ((size_t)(slot0 + p) * kTiles + h) * kRows + row).x);
+            }
+            const bool write = ok && row_ok && my_pos < bad && M != -INFINITY;
+            float L = 0.f;
+            for (int p = 0; p < nparts; ++p) {
+              const float2 v = __ldcg(a.part_ml + ((size_t)(slot0 + p) * kTiles + h) * kRows + row);
+              if (v.x != -INFINITY) L = fmaf(v.y, va::fast_exp2(v.x - M), L);
+            }
+            const float inv = L > 0.f ? 1.f / L : 0.f;
+            if (write) {
+#pragma unroll 1
+              for (int c = 0; c < D; c += 32) {
+                float acc[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+                for (int p = 0; p < nparts; ++p) {
+                  const size_t q = (size_t)(slot0 + p) * kTiles + h;
+                  const float mp = __ldcg(a.part_ml + q * kRows + row).x;
+                  if (mp == -INFINITY) continue;
+                  const float e = va::fast_exp2(mp - M);
+                  const float *src = a.part_o + q * D * kRows + row + (size_t)c * kRows;
+#pragma unroll
+                  for (int i = 0; i < 32; ++i) acc[i] = fmaf(__ldcg(src + (size_t)i * kRows), e, acc[i]);
+                }
+                store32(c, acc, inv);
               }
             }
           }

@@ -1,6 +1,6 @@
 """Per-op device timing of the hot-path kernels on the benchmark shapes.
 
-  python -m vllm_apple_b200.perf --op {decode,mixed,rmsnorm,rope,silu_mul,all}
+  python -m vllm_apple_b200.perf --op {decode,mixed,prefill,rmsnorm,rope,silu_mul,topk,all}
                                  [--workload devstral_b128] [--iters 50] [--warmup 5]
 
 Each op runs ``warmup`` untimed then ``iters`` timed launches bracketed by CUDA
@@ -96,8 +96,11 @@ def run_decode(workload, iters, warmup, graph=False):
             timing="CUDA graph replay" if graph else "back-to-back launches")
 
 
-def run_mixed(iters, warmup):
-    m = make_mixed_case(device="cuda", seed=0)
+def run_mixed(iters, warmup, prefill_only=False, head_size=128):
+    kw = {} if head_size == 128 else dict(Hq=14, Hkv=2, D=64)
+    if prefill_only:
+        kw["num_decode"] = 0
+    m = make_mixed_case(device="cuda", seed=0, **kw)
     q, k, v = m.q.cuda(), m.k.cuda(), m.v.cuda()
     bt, ts, ps, sm = (m.block_table.cuda(), m.token_to_seq.cuda(), m.positions.cuda(),
                       m.slot_mapping.cuda())
@@ -114,7 +117,8 @@ def run_mixed(iters, warmup):
     ctx = [int(pos[m.token_to_seq.long() == s].max()) + 1 for s in range(len(m.seq_lens))]
     nbytes = (sum(ctx) * Hkv * D * 4 + m.num_tokens * (Hq + 2 * Hkv) * D * 2
               + m.num_tokens * Hq * D * 2 + m.num_tokens * Hkv * D * 4)
-    _report("mixed", sec, nbytes, flops, tokens=m.num_tokens)
+    _report("prefill" if prefill_only else "mixed", sec, nbytes, flops, tokens=m.num_tokens,
+            head_size=m.D)
 
 
 def run_elementwise(which, iters, warmup):
@@ -156,7 +160,10 @@ def run_topk(iters, warmup):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", default="all",
-                    choices=["decode", "mixed", "rmsnorm", "rope", "silu_mul", "topk", "all"])
+                    choices=["decode", "mixed", "prefill", "rmsnorm", "rope", "silu_mul", "topk",
+                             "all"])
+    ap.add_argument("--head-size", type=int, default=128, choices=[64, 128],
+                    help="mixed / prefill: 22B shape (128) or Qwen shape (64)")
     ap.add_argument("--workload", default="devstral_b128")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
@@ -167,7 +174,9 @@ def main():
     if a.op in ("decode", "all"):
         run_decode(a.workload, a.iters, a.warmup, a.graph)
     if a.op in ("mixed", "all"):
-        run_mixed(a.iters, a.warmup)
+        run_mixed(a.iters, a.warmup, head_size=a.head_size)
+    if a.op in ("prefill", "all"):
+        run_mixed(a.iters, a.warmup, prefill_only=True, head_size=a.head_size)
     if a.op in ("rmsnorm", "rope", "silu_mul", "all"):
         run_elementwise(a.op, a.iters, a.warmup)
     if a.op in ("topk", "all"):
