@@ -166,42 +166,11 @@ VA_DEVINL uint64_t fadd2(uint64_t a, uint64_t b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-VA_DEVINL uint64_t fsub2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
 VA_DEVINL float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
-// 2^x for a pair, x <= ~8, on the FMA pipe instead of the special-function
-// unit: x = n + f with n = round(x) (add/subtract 1.5 * 2^23), f in [-1/2, 1/2];
-// 2^f by a cubic fitted here for minimal relative error on [-1/2, 1/2]
-// (max relative error 7.6e-5, below fp16's half ulp 4.9e-4); 2^n enters as an
-// exponent-field add.  x is clamped to -126, where the result is below 2^-125
-// (the hardware path returns 0 there): both round to 0 in fp16.
-VA_DEVINL uint64_t exp2_poly2(uint64_t x) {
-  float a, b;
-  upk2(x, a, b);
-  x = pk2(fmaxf(a, -126.f), fmaxf(b, -126.f));
-  const uint64_t M = pk2(12582912.f, 12582912.f);
-  const uint64_t t = fadd2(x, M);
-  const uint64_t f = fsub2(x, fsub2(t, M));
-  uint64_t y = ffma2(pk2(0.05517050251364708f, 0.05517050251364708f), f,
-                     pk2(0.24260824918746948f, 0.24260824918746948f));
-  y = ffma2(y, f, pk2(0.693260908126831f, 0.693260908126831f));
-  y = ffma2(y, f, pk2(0.9999282360076904f, 0.9999282360076904f));
-  float y0, y1, t0, t1;
-  upk2(y, y0, y1);
-  upk2(t, t0, t1);
-  // low bits of t hold n (two's complement); n << 23 lands in the exponent field
-  y0 = __uint_as_float(__float_as_uint(y0) + (__float_as_uint(t0) << 23));
-  y1 = __uint_as_float(__float_as_uint(y1) + (__float_as_uint(t1) << 23));
-  return pk2(y0, y1);
-}
-
 // ---- descriptors ------------------------------------------------------------
 // Shared-memory matrix descriptor, 128-byte swizzle (canonical 8-row x 128 B
 // atoms, atoms 1024-byte aligned).  lbo/sbo in bytes.
@@ -588,16 +557,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           {
             wait_bar(&bar_s[2 * h + (j & 1)], (uint32_t)((j >> 1) & 1));
             fence_after_sync();
-            uint32_t sr[32];
+            // both halves of the row's 64 scores in flight, then one wait
+            uint32_t sr[32], sr2[32];
             const uint32_t tS = tmem + (2 * h + (j & 1)) * kKeys + lane_base;
             tmem_ld32(tS, sr);
+            tmem_ld32(tS + 32, sr2);
             tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 32; ++c) p[c] = __uint_as_float(sr[c]);
-            tmem_ld32(tS + 32, sr);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) p[32 + c] = __uint_as_float(sr[c]);
+            for (int c = 0; c < 32; ++c) {
+              p[c] = __uint_as_float(sr[c]);
+              p[32 + c] = __uint_as_float(sr2[c]);
+            }
           }
           float alpha;
           {
@@ -621,21 +591,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             const bool none = mn == -INFINITY;
             alpha = (none || mn == m) ? 1.f : va::fast_exp2(m - mn);
             const float nmn = none ? 0.f : -mn;
-            // p = 2^(s * scale - m) in pairs; every third pair on the FMA pipe (the
-            // special-function unit is the softmax's bottleneck)
+            // p = 2^(s * scale - m) in pairs: the exponent argument by a packed FMA, the
+            // power by the special-function unit (measured on B200: evaluating a third
+            // of them by a polynomial on the FMA pipe instead cost 1.5 %: the softmax
+            // is bound by issue and latency, not by that unit)
             const uint64_t sc2 = pk2(a.scale_log2, a.scale_log2), nm2 = pk2(nmn, nmn);
             uint64_t sum2[2] = {pk2(0.f, 0.f), pk2(0.f, 0.f)};
 #pragma unroll
             for (int c = 0; c < kKeys / 2; ++c) {
               const uint64_t x = ffma2(pk2(p[2 * c], p[2 * c + 1]), sc2, nm2);
-              uint64_t e;
-              if (c % 3 == 2) {
-                e = exp2_poly2(x);
-              } else {
-                float x0, x1;
-                upk2(x, x0, x1);
-                e = pk2(va::fast_exp2(x0), va::fast_exp2(x1));
-              }
+              float x0, x1;
+              upk2(x, x0, x1);
+              const uint64_t e = pk2(va::fast_exp2(x0), va::fast_exp2(x1));
               upk2(e, p[2 * c], p[2 * c + 1]);
               sum2[c & 1] = fadd2(sum2[c & 1], e);
             }
