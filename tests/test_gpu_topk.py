@@ -136,3 +136,30 @@ def test_topk_matches_torch_topk_on_distinct_values(T, V, k):
     tv, ti = torch.topk(dx.float(), k, dim=1, largest=True, sorted=True)
     assert torch.equal(idx.long(), ti)
     assert torch.equal(val.float(), tv)
+
+
+@pytest.mark.parametrize("V", [131072, 24581, 100000])
+def test_topk_many_rows_edge_rows(V):
+    """Many rows (more than SMs: one CTA per row) including the rows that leave the
+    bound-and-screen path: a row of equal values (candidate overflow), a row whose
+    first logits are all -inf, NaN / -inf / +inf, ascending values, and (with a
+    padded row stride) a ragged tail of fewer than 8 logits; also through the
+    no-workspace entry point."""
+    T, k = 200, 64
+    x = _logits(V + 5, T, V, special=True)
+    x[3] = torch.arange(V, dtype=torch.float32).div(V / 60000.0).sub(30000).half()  # ascending
+    x[4, :9000] = float("-inf")                       # a long -inf prefix
+    x[5] = 1.5                                        # all equal
+    _check(x, k, stride=None if V % 8 == 0 else V + 8 - V % 8)  # aligned rows, ragged tail
+    # the no-workspace entry point
+    ops = _ops()
+    from vllm_apple_b200 import _lib
+    xs = x[:7].contiguous()
+    dx = xs.cuda()
+    idx = torch.empty(7, k, dtype=torch.int32, device="cuda")
+    val = torch.empty(7, k, dtype=torch.float16, device="cuda")
+    _lib.check(_lib.load().va_topk(idx.data_ptr(), val.data_ptr(), dx.data_ptr(), 7, V, V, k,
+                                   torch.cuda.current_stream().cuda_stream), "va_topk")
+    ei, ev = ref.topk(xs.numpy(), k)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ei)
+    np.testing.assert_array_equal(val.cpu().view(torch.int16).numpy(), ev.view(np.int16))

@@ -343,7 +343,12 @@ __global__ void __launch_bounds__(kNW * 32, decode_min_blocks<D, GC>())
     const int slot = k % kStages;
     const uint32_t parity = (uint32_t)(k / kStages) & 1u;
     if (!va::mbar_wait_bounded(&bars[warp * kStages + slot], parity, dead ? 64u : kWaitLimit)) {
-      if (!dead && lane == 0) va::raise_flag(a.err, VA_FLAG_WAIT_TIMEOUT);
+      if (!dead && lane == 0) {
+        va::raise_flag(a.err, VA_FLAG_WAIT_TIMEOUT);
+#ifdef VA_DIAG_SITES  // diagnostic builds: bit 20 decode, bit 21 one-token prefill rows
+        va::raise_flag(a.err, 0x100 << (a.rows ? 13 : 12));
+#endif
+      }
       dead = true;
     }
     const int64_t page = pbeg + warp + (int64_t)k * kNW;

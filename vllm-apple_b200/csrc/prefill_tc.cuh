@@ -267,12 +267,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int CPR = D / 8;  // 16-byte pieces per row
 
   auto dead = [&]() { return *(volatile int *)&s_dead != 0; };
-  auto timeout = [&]() {
+  // A build with -DVA_DIAG_SITES also sets bit 8 + site of the error word, naming
+  // the wait that gave up: 0 producer / stage free, 1-2 producer teardown, 3 MMA /
+  // chunk landed, 4 MMA / P published, 5 MMA teardown, 6 softmax / S written,
+  // 7 softmax / PV before a rescale, 8 softmax / last PV.
+  auto timeout = [&](int site = 15) {
+#ifdef VA_DIAG_SITES
+    va::raise_flag(a.err, 0x100 << site);
+#endif
     if (atomicExch(&s_dead, 1) == 0) va::raise_flag(a.err, VA_FLAG_WAIT_TIMEOUT);
   };
-  auto wait_bar = [&](uint64_t *bar, uint32_t parity) {
+  auto wait_bar = [&](uint64_t *bar, uint32_t parity, int site = 15) {
     if (dead()) return;
-    if (!va::mbar_wait_bounded(bar, parity, kWaitLimit)) timeout();
+    if (!va::mbar_wait_bounded(bar, parity, kWaitLimit)) timeout(site);
   };
   bool inited = false;  // thread 0: the mbarriers hold an earlier item's state
 
@@ -368,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           g_next = load_group(gi + 1);
         }
         const int32_t gid = __shfl_sync(0xffffffffu, g_cur, (first & 31) + (lane & (npc - 1)));
-        if (i >= kStages) wait_bar(&bar_empty[buf], (uint32_t)(((i / kStages) - 1) & 1));
+        if (i >= kStages) wait_bar(&bar_empty[buf], (uint32_t)(((i / kStages) - 1) & 1), 0);
         // page ids of this chunk (lane p holds page p)
         int32_t id = -1;
         const int page = first + lane;
@@ -434,9 +441,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) {
         for (int c = nch - kStages < 0 ? 0 : nch - kStages; c < nch; ++c) {
           const uint32_t par = (uint32_t)((c / kStages) & 1);
-          if (!va::mbar_wait_bounded(&bar_full[c % kStages], par, kWaitLimit)) timeout();
+          if (!va::mbar_wait_bounded(&bar_full[c % kStages], par, kWaitLimit)) timeout(1);
           if (!dead() && !va::mbar_wait_bounded(&bar_empty[c % kStages], par, kWaitLimit))
-            timeout();
+            timeout(2);
         }
       }
       __syncwarp();
@@ -474,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t IDESC_S = idesc_f16(kRows, kKeys, false);
         constexpr uint32_t IDESC_O = idesc_f16(kRows, D, true);
         auto wait_chunk = [&](int c) {
-          wait_bar(&bar_full[c % kStages], (uint32_t)((c / kStages) & 1));
+          wait_bar(&bar_full[c % kStages], (uint32_t)((c / kStages) & 1), 3);
         };
         // S_h(j) = Q_h K_j^T: A = Q_h [128 x D] K-major, B = K chunk [64 x D] K-major.
         auto issue_s = [&](int j) {
@@ -497,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // thread into the same buffer, executes after this MMA has read P (one
         // thread's tcgen05.mma operations run in issue order).
         auto issue_pv = [&](int j) {
-          wait_bar(&bar_p[h], (uint32_t)(j & 1));
+          wait_bar(&bar_p[h], (uint32_t)(j & 1), 4);
           if (lane == 0 && !dead()) {
             fence_after_sync();
             const uint32_t vbase = sV + (j % kStages) * S::kKV;
@@ -534,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // teardown: every MMA issued by this thread has retired
         if (lane == 0) {
           umma_commit(&bar_done[h]);
-          if (!va::mbar_wait_bounded(&bar_done[h], 0, kWaitLimit)) timeout();
+          if (!va::mbar_wait_bounded(&bar_done[h], 0, kWaitLimit)) timeout(5);
         }
         __syncwarp();
         all_sync();
@@ -555,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < nj; ++j) {
           float p[kKeys];
           {
-            wait_bar(&bar_s[2 * h + (j & 1)], (uint32_t)((j >> 1) & 1));
+            wait_bar(&bar_s[2 * h + (j & 1)], (uint32_t)((j >> 1) & 1), 6);
             fence_after_sync();
             // both halves of the row's 64 scores in flight, then one wait
             uint32_t sr[32], sr2[32];
@@ -616,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // once PV_h(j-1) is done with O.  P_h(j) goes to S_h(j)'s own buffer, which
           // no pending MMA reads, so without a rescale there is nothing to wait for.
           if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
-            wait_bar(&bar_pv[h], (uint32_t)((j - 1) & 1));
+            wait_bar(&bar_pv[h], (uint32_t)((j - 1) & 1), 7);
             fence_after_sync();
 #pragma unroll 1
             for (int c = 0; c < D; c += 32) {
@@ -642,7 +649,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           va::mbar_arrive(&bar_p[h]);
         }
         if (nj > 0) {
-          wait_bar(&bar_pv[h], (uint32_t)((nj - 1) & 1));
+          wait_bar(&bar_pv[h], (uint32_t)((nj - 1) & 1), 8);
           fence_after_sync();
         }
         // ---- epilogue: O / l -> fp16 rows, once every role is done ----
