@@ -78,8 +78,11 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            # nvidia-smi takes a moment to start; samples must cover the timed region,
+            # which for short runs (many GPUs, few steps) lasts only tens of ms
+            time.sleep(0.5)
         except OSError:
             self.proc = None
         return self
@@ -672,8 +675,8 @@ def run_row(args, rank, local):
     dev = torch.device("cuda", local)
     from vllm_apple_b200 import ops
     step, nbytes, flops, launches, cfg, cpu = row_case(args.row, dev)
-    # enough calls that the timed region lasts >= 0.8 s and so spans several clock
-    # samples (taken 100 ms apart)
+    # enough calls that the timed region lasts >= 0.8 s and so spans many clock
+    # samples (taken 20 ms apart)
     est = time_rotating(step, 20, args.warmup) / 20
     args.steps = max(args.steps, int(800.0 / max(est, 1e-3)) + 1)
     with ClockSampler(local) as clk:
