@@ -59,3 +59,22 @@ def test_oracle_padding_and_specials():
     i, v = ref.topk(x, 6)
     assert i.tolist() == [[3, 2, 5, 4, -1, -1]]
     assert np.isinf(v[0, 4]) and v[0, 4] < 0 and np.isinf(v[0, 0]) and v[0, 0] > 0
+
+
+@pytest.mark.parametrize("T,V,k", [(3, 32000, 50), (2, 151936, 40), (4, 5000, 1)])
+def test_oracle_matches_reference_cpu_sampler_topk(T, V, k):
+    """The reference's own CPU sampler takes top-k with ``torch.topk(req_logits, top_k)``
+    (vllm_apple/v1/worker/apple_model_runner.py:1799-1804).  On rows of distinct finite
+    values the selection is unique, so the oracle's indices and values must equal it."""
+    import torch
+    rng = np.random.default_rng(T + V + k)
+    bits = np.arange(-30000, 30000, dtype=np.int32).astype(np.int16).view(np.float16)
+    pool = np.unique(bits[np.isfinite(bits)].astype(np.float32)).astype(np.float16)
+    x = np.stack([rng.permutation(pool)[:V] if V <= pool.size else
+                  np.concatenate([rng.permutation(pool),
+                                  np.full(V - pool.size, -np.inf, np.float16)])
+                  for _ in range(T)])
+    i, v = ref.topk(x, k)
+    tv, ti = torch.topk(torch.from_numpy(x.astype(np.float32)), k, dim=1)
+    np.testing.assert_array_equal(i, ti.numpy())
+    np.testing.assert_array_equal(v.astype(np.float32), tv.numpy())
