@@ -238,8 +238,52 @@ def golden_norm_silu():
                         silu_mul=silu)
 
 
+def golden_decode_configs(mps):
+    """The reference's decode on the exact config-1 step (qwen_b4, seed 0, as
+    vllm_apple_b200.workloads builds it) and on one 22B-shaped sequence of 600 tokens
+    (32q/8kv heads, D = 128, GQA 4:1; the config-3 shape, one sequence to keep the
+    fixture small)."""
+    sys.path.insert(0, os.path.join(REPO, "vllm-apple_b200"))
+    from vllm_apple_b200.workloads import DecodeCase, assign_blocks, make_decode_case
+    cases = {"decode_config1.npz": make_decode_case("qwen_b4", seed=0, layout="nhd")}
+    gen = torch.Generator().manual_seed(3)
+    L = torch.tensor([600])
+    bt, nb = assign_blocks(L.tolist(), 16, 0, gen)
+    slot = bt[0, 599 // 16].to(torch.int64).reshape(1) * 16 + 599 % 16
+    cases["decode_22b_600.npz"] = DecodeCase(
+        "22b", 32, 8, 128, 16, "nhd", nb, L.to(torch.int32), bt, slot,
+        torch.randn(1, 32, 128, generator=gen).half(), torch.randn(1, 8, 128, generator=gen).half(),
+        torch.randn(1, 8, 128, generator=gen).half(),
+        torch.randn(nb, 16, 8, 128, generator=gen).half(),
+        torch.randn(nb, 16, 8, 128, generator=gen).half())
+    for name, c in cases.items():
+        B = c.batch
+        cache = torch.stack([c.k_cache, c.v_cache])
+        L = c.seq_lens.tolist()
+        bt = c.block_table.to(torch.int64)
+        meta = make_meta(mps, B, list(range(B + 1)), L, bt, c.slot_mapping, B)
+        c16 = cache.clone()
+        run_forward(mps, c.Hq, c.Hkv, c.D, c.q, c.new_k, c.new_v, c16, meta)  # KV bytes
+        c32 = cache.float()
+        out = run_forward(mps, c.Hq, c.Hkv, c.D, c.q.float(), c.new_k.float(), c.new_v.float(),
+                          c32, meta)
+        # the reference wrote exactly the B slots; keep the rows it wrote (not the
+        # whole second cache) to keep the fixture small
+        ci, co = cache.numpy(), c16.numpy()
+        sl = c.slot_mapping.numpy()
+        blk, off = sl // c.bs, sl % c.bs
+        diff = np.zeros(ci.shape[1:3], bool)
+        diff[blk, off] = True
+        assert np.array_equal(ci.view(np.int16)[:, ~diff], co.view(np.int16)[:, ~diff])
+        np.savez_compressed(os.path.join(HERE, name), q=c.q.numpy(), k=c.new_k.numpy(),
+                            v=c.new_v.numpy(), cache_in=ci, written_rows=co[:, blk, off],
+                            block_table=c.block_table.numpy(), seq_lens=c.seq_lens.numpy(),
+                            slot_mapping=sl, out=out.numpy().astype(np.float32))
+
+
 def main():
     mps = load_reference_attention()
+    golden_decode_configs(mps)
     golden_decode(mps)
     golden_mixed(mps)
     golden_prefill(mps)

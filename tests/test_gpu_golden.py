@@ -72,3 +72,26 @@ def test_rope_equivalence_with_reference_test_formula():
     # the reference test's 1e-3, plus the fp16 rounding of the output (half an ulp)
     assert bool(((dq.cpu().float() - qe).abs() <= 1e-3 + 2 ** -11 * qe.abs()).all())
     assert bool(((dk.cpu().float() - ke).abs() <= 1e-3 + 2 ** -11 * ke.abs()).all())
+
+
+@pytest.mark.parametrize("name,D", [("decode_config1.npz", 64), ("decode_22b_600.npz", 128)])
+def test_decode_config_goldens_on_gpu(name, D):
+    """The fused decode on the reference-produced config-1 step and 22B-shaped sequence:
+    KV bytes equal the reference's, outputs within 2e-3 of its fp32 result."""
+    from vllm_apple_b200 import ops
+    g = dict(np.load(os.path.join(GOLD, name)))
+    cache = torch.from_numpy(g["cache_in"]).cuda()
+    kc, vc = cache[0], cache[1]
+    q = torch.from_numpy(g["q"]).cuda()
+    out = torch.empty_like(q)
+    ops.paged_decode(out, q, kc, vc, torch.from_numpy(g["block_table"]).cuda(),
+                     torch.from_numpy(g["seq_lens"]).cuda(), scale=1 / np.sqrt(D),
+                     max_seq_len=int(g["seq_lens"].max()), new_k=torch.from_numpy(g["k"]).cuda(),
+                     new_v=torch.from_numpy(g["v"]).cuda(), layout="nhd")
+    assert ops.check_device_errors() == 0
+    assert max_abs(np16(out), g["out"]) <= ATOL
+    exp = g["cache_in"].copy()
+    bs = exp.shape[2]
+    sl = g["slot_mapping"]
+    exp[:, sl // bs, sl % bs] = g["written_rows"]
+    np.testing.assert_array_equal(bits(cache), exp.view(np.int16))

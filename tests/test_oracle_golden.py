@@ -205,3 +205,28 @@ def test_known_answer_layout_roundtrip():
         else:
             assert np.all(kc[3, 5] == 1.5) and np.all(vc[3, 5] == 2.5)
         assert kc.sum() == 1.5 * H * D and vc.sum() == 2.5 * H * D
+
+
+def _expected_cache(g):
+    """cache_in with the rows the reference wrote at the new tokens' slots."""
+    c = g["cache_in"].copy()
+    bs = c.shape[2]
+    sl = g["slot_mapping"]
+    c[:, sl // bs, sl % bs] = g["written_rows"]
+    return c
+
+
+@pytest.mark.parametrize("name,D", [("decode_config1.npz", 64), ("decode_22b_600.npz", 128)])
+def test_decode_config_goldens(name, D):
+    """Config 1 exactly (qwen_b4, seed 0) and a 22B-shaped 600-token sequence, as the
+    reference's MPSAttentionImpl.forward computed them: the oracle's KV write lands on
+    the same bytes and its attention matches the reference's fp32 output."""
+    g = load(name)
+    kc, vc = g["cache_in"][0].copy(), g["cache_in"][1].copy()
+    ref.kv_write_decode(kc, vc, g["k"], g["v"], g["block_table"], g["seq_lens"], layout="nhd")
+    exp = _expected_cache(g)
+    assert np.array_equal(kc.view(np.int16), exp[0].view(np.int16))
+    assert np.array_equal(vc.view(np.int16), exp[1].view(np.int16))
+    o = ref.paged_decode(g["q"], kc, vc, g["block_table"], g["seq_lens"], 1 / np.sqrt(D),
+                         layout="nhd")
+    assert np.max(np.abs(o - g["out"])) < 2e-5
