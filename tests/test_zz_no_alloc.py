@@ -24,7 +24,7 @@ def _args(c, out, q, kc, vc, bt, sl, max_len):
             c.scale, H * bs * D, bs * D, D, c.Hq * D, D, c.Hq * D, D, 0, 0)
 
 
-@pytest.mark.parametrize("config,batch", [("devstral_b128", 24), ("qwen_b64", None)])
+@pytest.mark.parametrize("config,batch", [("devstral_b128", 24), ("qwen_b64", None), ("devstral_b128", 256)])
 def test_noalloc_decode_matches_workspace_decode(config, batch):
     from vllm_apple_b200 import _lib, ops
     from vllm_apple_b200.workloads import make_decode_case
