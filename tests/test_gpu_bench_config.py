@@ -3,10 +3,9 @@
 ``bench.py`` times the fused decode (KV write + attention, engine layout) of
 the 22B-shaped batch of 1024 sequences on one GPU, and the LPT shards of that
 batch on 2, 4 and 8 GPUs (each rank builds its shard with
-``make_decode_case(..., seq_subset=shard, lengths=L_all)``).  The split-KV plan
-differs between them (one split per sequence at 1024 sequences, several at the
-128..512-sequence shards), so each case runs here exactly as the bench builds
-it:
+``make_decode_case(..., seq_subset=shard, lengths=L_all)``).  Each case runs
+here exactly as the bench builds it (all of them large enough to run unsplit,
+longest sequence first, through the on-device ordering):
 
 * KV write: the whole K and V caches after the call equal the caches before
   it with the new rows written at ``seq_len - 1`` (bit-exact; every untouched
