@@ -116,8 +116,8 @@ VA_API int va_write_kv_batch(uint16_t *key_dst, uint16_t *value_dst, const uint1
 
 /* Bytes of workspace va_paged_decode needs for this shape (0 when no sequence
  * needs neither split-KV partials nor an ordering).  The workspace holds fp32
- * split partials and, for large batches (at least 1024 sequence x kv-head CTAs,
- * 2048 at head_size <= 64), the longest-first order of the sequences (written
+ * split partials and, for large batches (at least 1024 sequence x kv-head CTAs),
+ * the longest-first order of the sequences (written
  * by the call itself); it needs no initialisation.  Calls that share a workspace
  * must not overlap on the GPU (stream order is enough). */
 VA_API size_t va_paged_decode_workspace_size(int64_t num_seqs, int num_query_heads, int num_kv_heads,

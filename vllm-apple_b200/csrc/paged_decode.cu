@@ -664,8 +664,10 @@ __global__ void __launch_bounds__(1024) order_by_length_kernel(const int32_t *se
 
 // Whether a grid of `units` (sequence, kv head, q-head group) CTAs runs longest first
 // (VA_DECODE_ORDER=0 / 1 forces never / always).  With enough units the ordered grid is
-// an LPT schedule and needs no splitting (see make_plan); below that, splits keep the
-// SMs busy and the order does not pay for its extra launch.
+// an LPT schedule (at head_size > 64 it then needs no splitting, see make_plan); below
+// that the order does not pay for its extra launch (measured: Qwen shape batch 64
+// 28.5 -> 32.2 us, 22B batch 64 124 -> 131 us with it; Qwen batch 512, 1024 units,
+// 155 -> 141 us).
 bool order_enabled(int64_t units, int head_size) {
   static int env = -2;
   if (env == -2) {
@@ -673,7 +675,7 @@ bool order_enabled(int64_t units, int head_size) {
     env = e ? atoi(e) : -1;
   }
   if (env >= 0) return env != 0;
-  return units >= (head_size <= 64 ? 2048 : 1024);
+  return units >= 1024;
 }
 
 // ---------------------------------------------------------------------------
@@ -707,12 +709,14 @@ Plan make_plan(int64_t num_seqs, int Hq, int Hkv, int head_size, int block_size,
   }
   int pps = env_pps;
   p.ordered = allow_order && order_enabled(base, head_size);
-  if (pps <= 0 && p.ordered) {
+  if (pps <= 0 && p.ordered && head_size > 64) {
     // Longest first with at least ~2 waves of CTAs: an LPT schedule of whole sequences
     // balances the SMs by itself; splitting only adds partials, a combine and more
     // CTAs.  Measured on B200 (22B shape, us): 128 sequences 230 -> 200, the 128-, 256-
     // and 512-sequence shards of the batch of 1024 232 -> 203, 418 -> 392, 812 -> 783;
-    // pages per split 128 / 256 gave 216 / 214 at 128 sequences.
+    // pages per split 128 / 256 gave 216 / 214 at 128 sequences.  At head_size <= 64
+    // (many q heads per kv head, compute-heavy pages) splitting still pays: Qwen shape
+    // batch 256 unsplit 101 us against 83 us split.
     pps = 512;
   } else if (pps <= 0) {
     // Largest split (fewest partials, fewest idle CTAs) whose worst-case CTA count
