@@ -226,6 +226,9 @@ __global__ void __launch_bounds__(kNW * 32, decode_min_blocks<D, GC>())
   // the combine kernel (launched with programmatic dependency) may be scheduled now;
   // it waits for this grid's completion before reading any partial
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  // with an order, this grid is a programmatic dependent of the ordering kernel:
+  // wait until that grid has completed and its order is visible
+  if (a.order) asm volatile("griddepcontrol.wait;" ::: "memory");
   // index of the partials; the sequence outside row mode, taken longest first when
   // an order is given (long CTAs first: the grid's tail is made of short ones)
   const int seq = a.order ? a.order[blockIdx.z] : (int)blockIdx.z;
@@ -627,6 +630,8 @@ constexpr int kOrderBuckets = 1024;
 __global__ void __launch_bounds__(1024) order_by_length_kernel(const int32_t *seq_lens,
                                                               int64_t num_seqs, int bs,
                                                               int32_t *order) {
+  // the decode grid may launch now; it waits for this grid's completion
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __shared__ int hist[kOrderBuckets];
   __shared__ int warp_buf[32];
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -774,7 +779,24 @@ int launch_t(const DecodeArgs &a, dim3 grid, cudaStream_t st) {
       return VA_ERR_LAUNCH;
     configured[dev].store(1, std::memory_order_release);
   }
-  paged_decode_kernel<D, GC, BS><<<grid, kNW * 32, C::kSmem, st>>>(a);
+  if (a.order) {
+    // launched as a programmatic dependent of the ordering kernel, so its launch
+    // overlaps that kernel (it waits for the order before reading it)
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kNW * 32);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, paged_decode_kernel<D, GC, BS>, a) != cudaSuccess)
+      return VA_ERR_LAUNCH;
+  } else {
+    paged_decode_kernel<D, GC, BS><<<grid, kNW * 32, C::kSmem, st>>>(a);
+  }
   if (grid.x > 1) {
     const int st0 = va_host::launch_status();
     if (st0 != VA_OK) return st0;
