@@ -725,13 +725,22 @@ Plan make_plan(int64_t num_seqs, int Hq, int Hkv, int head_size, int block_size,
     pps = 512;
   } else if (pps <= 0) {
     // Largest split (fewest partials, fewest idle CTAs) whose worst-case CTA count
-    // still reaches a head-size-dependent floor; measured on B200 (batch 128 ->
-    // 64 pages, batch 1024 -> 512, Qwen-shape batch 64 -> 16).
-    const int64_t floor_units = head_size >= 128 ? 8192 : (head_size >= 96 ? 4096 : 2048);
+    // still reaches 2048, and at head_size <= 64 at least 8 pages per split unless the
+    // grid is tiny (fewer than 32 sequence x kv-head units: Qwen batch 4 runs best at 4).
+    // Measured on B200 (graph replay, us; the earlier floors 8192 at head_size 128,
+    // 2048 at 64, no minimum -> this rule): 22B shape batch 16 88.4 -> 44.3, batch 32
+    // 96.8 -> 62.2 (32 / 64 pages per split instead of 4 / 8); Qwen shape batch 16
+    // 20.5 -> 14.6 (8 instead of 4); unchanged at Qwen batch 64 and 256.
+    // The one-token rows of a prefill batch keep the earlier, higher floors: their
+    // grid is sized by an upper bound of the rows, so `base` overstates the CTAs
+    // (config-4 mixed step: 321 us with them, 350 us with 2048).
+    const int64_t floor_units =
+        allow_order ? 2048 : (head_size >= 128 ? 8192 : (head_size >= 96 ? 4096 : 2048));
+    const int min_pps = (allow_order && head_size <= 64 && base >= 32) ? 8 : 4;
     const int choices[] = {512, 256, 128, 64, 32, 16, 8, 4};
-    pps = 4;
+    pps = min_pps;
     for (int c : choices)
-      if (base * ((npmax + c - 1) / c) >= floor_units) { pps = c; break; }
+      if (c >= min_pps && base * ((npmax + c - 1) / c) >= floor_units) { pps = c; break; }
   }
   p.pps = pps;
   const int64_t ms = npmax > 0 ? (npmax + pps - 1) / pps : 1;
