@@ -54,11 +54,11 @@ def peaks():
 
 # DRAM bytes (read + write) per decode launch over its algorithmic bytes, from one
 # ncu capture (dram__bytes_read.sum + dram__bytes_write.sum of one launch of the
-# devstral_b128 decode: 1.293 GB read + 5.7 MB written for 1.291 GB algorithmic;
-# 1.3 GB of KV, well above L2); the traffic reported for a launch is this ratio
-# times that launch's algorithmic bytes (traffic grows with the KV bytes read,
-# which the algorithmic bytes count once).
-DECODE_TRAFFIC_RATIO = 1.0062
+# devstral_b128 decode, longest first and unsplit: 1.2933 GB read + 3.6 MB written
+# for 1.2910 GB algorithmic; 1.3 GB of KV, well above L2); the traffic reported
+# for a launch is this ratio times that launch's algorithmic bytes (traffic grows
+# with the KV bytes read, which the algorithmic bytes count once).
+DECODE_TRAFFIC_RATIO = 1.0046
 DECODE_TRAFFIC_CAPTURE = "ncu, devstral_b128 decode, one launch, scaled by algorithmic bytes"
 
 
