@@ -89,3 +89,22 @@ def test_ops_refuse_cpu_tensors():
     x = torch.zeros(4, 8, dtype=torch.float16)
     with pytest.raises(RuntimeError, match="CUDA"):
         ops.silu_mul(x, x, x)
+
+
+def test_decode_plan_regimes(lib):
+    """The planner's two regimes, seen through the workspace they need (host-side,
+    no GPU): a grid of >= 1024 (sequence, kv head) CTAs runs longest first and, at
+    head_size > 64, unsplit below 8192 tokens -- its workspace is only the order
+    (one int per sequence, 256-byte aligned); smaller grids split and need fp32
+    partials (acc + (m, l) per sequence, q head and split)."""
+    f = lib.va_paged_decode_workspace_size
+    # 22B shape, 128 sequences x 8 kv heads = 1024 CTAs: ordered, unsplit
+    assert f(128, 32, 8, 128, 16, 8192) == 512
+    assert f(1024, 32, 8, 128, 16, 8192) == 4096
+    # ... but contexts past 512 pages still split (partials + order)
+    assert f(128, 32, 8, 128, 16, 16384) > 128 * 32 * 2 * 128 * 4
+    # 64 sequences (512 CTAs): split rule, 128 pages per split at 8192 tokens
+    assert f(64, 32, 8, 128, 16, 8192) == 64 * 32 * 4 * 128 * 4 + 64 * 32 * 4 * 2 * 4
+    # Qwen shape at 1024 units stays split (and ordered): partials + order
+    w = f(512, 14, 2, 64, 16, 4096)
+    assert w > 512 * 4 and (w - ((512 * 4 + 255) // 256) * 256) % 256 == 0
