@@ -14,6 +14,14 @@ namespace va {
 // ---------------------------------------------------------------------------
 // error flag
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch, device side: let the next grid on the stream be
+// scheduled now, then wait for the previous grid's completion and memory before
+// touching any input (a no-op wait when this grid was launched without the attribute).
+VA_DEVINL void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 VA_DEVINL void raise_flag(int32_t *flag, int32_t bits) {
   if (flag) atomicOr(flag, bits);
 }
@@ -161,6 +169,33 @@ inline int sm_count() {
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? VA_OK : VA_ERR_LAUNCH;
+}
+
+// <<<grid, block, 0, st>>> with the programmatic-stream-serialization attribute, so
+// the launch overlaps the tail of the kernel before it on the stream.
+// Every kernel launched this way must execute griddepcontrol.wait in all of its
+// CTAs before it exits (va::pdl_enter at entry), so that its completion still
+// implies the completion of everything before it on the stream.
+template <typename... KArgs, typename... Args>
+int launch_pdl_smem(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                    cudaStream_t st, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...) == cudaSuccess ? 0 : 1;
+}
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st,
+               Args &&...args) {
+  return launch_pdl_smem(kernel, grid, block, 0, st, static_cast<Args &&>(args)...);
 }
 
 }  // namespace va_host

@@ -11,34 +11,6 @@
 
 namespace {
 
-// Programmatic dependent launch: the next kernel on the stream (if launched with
-// the attribute) may be scheduled at once; this kernel waits for the previous
-// grid's completion (and its memory) before touching any input.  A previous
-// kernel that never triggers makes the wait return at its completion, as for a
-// plain launch.
-VA_DEVINL void pdl_enter() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-
-// <<<grid, block, 0, st>>> with the programmatic-stream-serialization attribute, so
-// the launch overlaps the tail of the kernel before it on the stream.
-template <typename... KArgs, typename... Args>
-void launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, cudaStream_t st,
-                Args &&...args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
-}
-
 VA_DEVINL void unpack8(const uint4 &v, float (&f)[8]) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -87,7 +59,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(
     __half *out, const __half *x, const __half *w, const __half *res, int64_t T, int64_t hidden,
     float eps, int64_t xs, int64_t os, int64_t rs) {
   __shared__ float red[2][kNormThreads / 32];  // alternating rows: one barrier per row
-  pdl_enter();
+  va::pdl_enter();
   const int nvec = (int)(hidden / 8);
   const uint4 *wr = reinterpret_cast<const uint4 *>(w);
   auto load = [&](int64_t row, uint4 (&v)[VPT]) {
@@ -184,10 +156,10 @@ void launch_norm_vec(bool r, int64_t T, cudaStream_t st, __half *o, const __half
                      const __half *w, const __half *res, int64_t h, float eps, int64_t xs,
                      int64_t os, int64_t rs) {
   if (r)
-    launch_pdl(rmsnorm_vec_kernel<VPT, true>, norm_grid<VPT, true>(T), kNormThreads, st, o, x,
+    va_host::launch_pdl(rmsnorm_vec_kernel<VPT, true>, norm_grid<VPT, true>(T), kNormThreads, st, o, x,
                w, res, T, h, eps, xs, os, rs);
   else
-    launch_pdl(rmsnorm_vec_kernel<VPT, false>, norm_grid<VPT, false>(T), kNormThreads, st, o,
+    va_host::launch_pdl(rmsnorm_vec_kernel<VPT, false>, norm_grid<VPT, false>(T), kNormThreads, st, o,
                x, w, res, T, h, eps, xs, os, rs);
 }
 
@@ -210,7 +182,7 @@ VA_DEVINL void rot_pair(float x0, float x1, float c, float s, float &y0, float &
 
 template <bool NEOX>
 __global__ void __launch_bounds__(256) rope_vec_kernel(const RopeArgs a) {
-  pdl_enter();
+  va::pdl_enter();
   const int half = a.rot / 2;
   const int groups = half / 8;
   const int heads = a.Hq + a.Hkv;
@@ -304,7 +276,7 @@ VA_DEVINL float silu_mul1_exact(float g, float u) {
 // thread per iteration.
 __global__ void __launch_bounds__(256) silu_mul_vec_kernel(uint4 *out, const uint4 *g,
                                                            const uint4 *u, int64_t nvec) {
-  pdl_enter();
+  va::pdl_enter();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nvec; i += 2 * stride) {
     const int64_t i2 = i + stride;
@@ -411,8 +383,8 @@ extern "C" int va_rope(void *q, void *k, const float *cos_cache, const float *si
   const int heads = num_heads + num_kv_heads;
   if (vec) {
     const unsigned g = grid_for(num_tokens * heads * (half / 8), 256);
-    if (is_neox) launch_pdl(rope_vec_kernel<true>, g, 256, st, a);
-    else launch_pdl(rope_vec_kernel<false>, g, 256, st, a);
+    if (is_neox) va_host::launch_pdl(rope_vec_kernel<true>, g, 256, st, a);
+    else va_host::launch_pdl(rope_vec_kernel<false>, g, 256, st, a);
   } else {
     const unsigned g = grid_for(num_tokens * heads * half, 256);
     if (is_neox) rope_any_kernel<true><<<g, 256, 0, st>>>(a);
@@ -430,7 +402,7 @@ extern "C" int va_silu_mul(void *out, const void *gate, const void *up, int64_t 
   if (num_elements % 8 == 0 && va_host::aligned16(out) && va_host::aligned16(gate) &&
       va_host::aligned16(up)) {
     const int64_t nvec = num_elements / 8;
-    launch_pdl(silu_mul_vec_kernel, grid_for(nvec, 256), 256, st,
+    va_host::launch_pdl(silu_mul_vec_kernel, grid_for(nvec, 256), 256, st,
         static_cast<uint4 *>(out), static_cast<const uint4 *>(gate),
         static_cast<const uint4 *>(up), nvec);
   } else {

@@ -96,6 +96,7 @@ __global__ void __launch_bounds__(1024) plan_tiles_kernel(const int32_t *token_t
   __shared__ int warp_buf[32];
   __shared__ int carry_max, carry_sum, n_single;
   __shared__ int bucket[kOrderBuckets];
+  va::pdl_enter();
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   if (tid == 0) { carry_max = 0; carry_sum = 0; n_single = 0; }
   __syncthreads();
@@ -604,7 +605,8 @@ int launch_tc_t(const tc::Args &a, const CUtensorMap &mk, const CUtensorMap &mv,
       return VA_ERR_LAUNCH;
     configured[dev] = 1;
   }
-  tc::paged_prefill_tc_kernel<D, GC><<<grid, tc::kThreads, S::kBytes, st>>>(a, mk, mv);
+  va_host::launch_pdl_smem(tc::paged_prefill_tc_kernel<D, GC>, grid, tc::kThreads, S::kBytes,
+                           st, a, mk, mv);
   return va_host::launch_status();
 }
 
@@ -840,10 +842,9 @@ extern "C" int va_paged_prefill(void *out, const void *q, const void *k_cache,
     up.slot_cap = pl.slot_cap;
     up.max_units = pl.max_units;
   }
-  plan_tiles_kernel<<<1, 1024, 0, st>>>(token_to_seq, positions, num_tokens, TQ, tiles, tiles_n,
-                                        mt, pl.route ? singles : nullptr,
-                                        pl.route ? singles_n : nullptr,
-                                        use_tc ? order : nullptr, err_flag, up);
+  va_host::launch_pdl(plan_tiles_kernel, 1, 1024, st, token_to_seq, positions, num_tokens, TQ,
+                      tiles, tiles_n, mt, pl.route ? singles : nullptr,
+                      pl.route ? singles_n : nullptr, use_tc ? order : nullptr, err_flag, up);
   if (va_host::launch_status() != VA_OK) return VA_ERR_LAUNCH;
   auto launch_rows = [&](cudaStream_t rs) {
     return va_internal::decode_rows(

@@ -253,6 +253,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   int *s_pos = reinterpret_cast<int *>(smem + S::oPos);  // [kTiles][kRows]
   __shared__ int s_ctx[kTiles], s_bad_from, s_dead, s_item[2], s_last;
 
+  // the planner's tiles, units and counter are read below: wait for it
+  va::pdl_enter();
   const int ny = a.Hkv * a.hgroups;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int BS = a.bs, TQ = a.TQ;

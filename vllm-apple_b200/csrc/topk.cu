@@ -228,6 +228,7 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
   __shared__ int s_bin, s_above, s_gt, s_ties;
   __shared__ unsigned long long cand[kCap];
   __shared__ int s_cnt;
+  va::pdl_enter();
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t off = (int64_t)blockIdx.y * slice;  // a multiple of 8 (host)
   const int64_t n = n_row - off < slice ? (n_row - off > 0 ? n_row - off : 0) : slice;
@@ -417,6 +418,7 @@ __global__ void __launch_bounds__(kThreads) topk_merge_kernel(int32_t *out_idx, 
                                                               const uint16_t *ws_val, int slices,
                                                               int k) {
   __shared__ unsigned long long cand[kMergeCap];
+  va::pdl_enter();
   const int tid = threadIdx.x;
   const int nc = slices * k;
   int m = 1;
@@ -481,7 +483,7 @@ extern "C" int va_topk_ws(int32_t *indices, void *values, const void *logits,
   const int vec = (va_host::aligned16(logits) && row_stride % 8 == 0) ? 1 : 0;
   auto st = static_cast<cudaStream_t>(stream);
   if (c < 2 || !vec) {  // one CTA per row
-    topk_kernel<<<dim3((unsigned)num_tokens, 1), kThreads, 0, st>>>(
+    va_host::launch_pdl(topk_kernel, dim3((unsigned)num_tokens, 1), kThreads, st,
         indices, static_cast<uint16_t *>(values), static_cast<const uint16_t *>(logits),
         vocab_size, row_stride, k, vec, vocab_size);
     return va_host::launch_status();
@@ -492,11 +494,11 @@ extern "C" int va_topk_ws(int32_t *indices, void *values, const void *logits,
   int32_t *ws_idx = static_cast<int32_t *>(workspace);
   uint16_t *ws_val = reinterpret_cast<uint16_t *>(static_cast<unsigned char *>(workspace) +
                                                   ((n * 4 + 255) / 256) * 256);
-  topk_kernel<<<dim3((unsigned)num_tokens, (unsigned)c), kThreads, 0, st>>>(
+  va_host::launch_pdl(topk_kernel, dim3((unsigned)num_tokens, (unsigned)c), kThreads, st,
       ws_idx, ws_val, static_cast<const uint16_t *>(logits), vocab_size, row_stride, k, vec,
       topk_slice_len(vocab_size, c));
   if (va_host::launch_status() != VA_OK) return VA_ERR_LAUNCH;
-  topk_merge_kernel<<<(unsigned)num_tokens, kThreads, 0, st>>>(
+  va_host::launch_pdl(topk_merge_kernel, (unsigned)num_tokens, kThreads, st,
       indices, static_cast<uint16_t *>(values), ws_idx, ws_val, c, k);
   return va_host::launch_status();
 }
@@ -509,8 +511,8 @@ extern "C" int va_topk(int32_t *indices, void *values, const void *logits, int64
   if (num_tokens == 0) return VA_OK;
   if (!indices || !values || !logits) return VA_ERR_INVALID_ARG;
   const int vec = (va_host::aligned16(logits) && row_stride % 8 == 0) ? 1 : 0;
-  topk_kernel<<<dim3((unsigned)num_tokens, 1), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      indices, static_cast<uint16_t *>(values), static_cast<const uint16_t *>(logits),
+  va_host::launch_pdl(topk_kernel, dim3((unsigned)num_tokens, 1), kThreads,
+                      static_cast<cudaStream_t>(stream), indices, static_cast<uint16_t *>(values), static_cast<const uint16_t *>(logits),
       vocab_size, row_stride, k, vec, vocab_size);
   return va_host::launch_status();
 }
