@@ -9,17 +9,20 @@
 // -inf.  Ties are resolved by the lower index (the reference's order between
 // equal values depends on its thread layout; values are identical either way).
 //
-// Design (HBM-bound: one read of the row from DRAM, a second from L2), one CTA
+// Design (HBM-bound: one read of the row from DRAM, a partial second from L2), one CTA
 // per row, on an order-preserving 16-bit key of the fp16 bits:
 //   * fast path (k <= 512): every thread takes the max of its slice (fp16 max
 //     over 16-byte vectors); the k-th largest of those maxima -- found by a
 //     binary search over the key bits with block-wide counts -- is a lower
 //     bound of the row's k-th largest key (the k maxima above it are k
 //     distinct logits), so the logits at or above it contain the answer, ties
-//     included.  A second pass screens 8 logits at a time with an fp16 compare
-//     against the bound and appends the few that pass to shared memory
-//     (warp-aggregated slots); the list is sorted by (key desc, index asc)
-//     with a bitonic sort and the first k written.
+//     included.  Only the ~k threads whose maximum reaches the bound can hold
+//     such logits: a second pass re-reads just their vectors (from L2), 8
+//     logits at a time with an fp16 compare against the bound, and appends the
+//     few that pass to shared memory (warp-aggregated slots).  Each candidate's
+//     rank in (key desc, index asc) order is the count of larger candidates
+//     (one thread per candidate; a bitonic sort for long lists), and the first
+//     k are written at their ranks.
 //   * exact path (k > 512, fewer than k threads holding a valid logit, or more
 //     than kCap logits passing the bound, e.g. a row of equal logits): a radix
 //     select -- 256-bin histograms of the high, then the low byte (per-warp
@@ -227,7 +230,8 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
   __shared__ int warp_sums[kWarps];
   __shared__ int s_bin, s_above, s_gt, s_ties;
   __shared__ unsigned long long cand[kCap];
-  __shared__ int s_cnt;
+  __shared__ int s_cnt, s_na;
+  __shared__ int s_list[kThreads];  // threads whose maximum reaches the bound
   va::pdl_enter();
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t off = (int64_t)blockIdx.y * slice;  // a multiple of 8 (host)
@@ -254,7 +258,10 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
         },
         [&](int64_t, uint32_t h) { mx = max(mx, key_of(h)); });
     mx = max(mx, max(key_of(as_u32(m2) & 0xFFFFu), key_of(as_u32(m2) >> 16)));
-    if (tid == 0) s_cnt = 0;
+    if (tid == 0) {
+      s_cnt = 0;
+      s_na = 0;
+    }
     // the k-th largest thread max = the largest x with #(maxima >= x) >= k
     uint32_t bound = 0;
 #pragma unroll 1
@@ -283,29 +290,74 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
           }
         }
       };
-      for_each8(
-          row, n, v, drop,
-          [&](int64_t i0, const uint4 &q) {
-            const unsigned act = __activemask();
-            const unsigned hit = __hge2_mask(as_h2(q.x), b2) | __hge2_mask(as_h2(q.y), b2) |
-                                 __hge2_mask(as_h2(q.z), b2) | __hge2_mask(as_h2(q.w), b2);
-            if (__any_sync(act, hit != 0u)) {
-              const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-              uint32_t pend = 0;
-              if (hit) {
+      auto screen8 = [&](int64_t i0, const uint4 &q) {
+        const unsigned act = __activemask();
+        const unsigned hit = __hge2_mask(as_h2(q.x), b2) | __hge2_mask(as_h2(q.y), b2) |
+                             __hge2_mask(as_h2(q.z), b2) | __hge2_mask(as_h2(q.w), b2);
+        if (__any_sync(act, hit != 0u)) {
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+          uint32_t pend = 0;
+          if (hit) {
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                  if (key_of((w[j >> 1] >> ((j & 1) * 16)) & 0xFFFFu) >= bound) pend |= 1u << j;
+            for (int j = 0; j < 8; ++j)
+              if (key_of((w[j >> 1] >> ((j & 1) * 16)) & 0xFFFFu) >= bound) pend |= 1u << j;
+          }
+          append(act, pend, w, i0);
+        }
+      };
+      auto screen1 = [&](int64_t i, uint32_t h) {
+        const uint32_t w[4] = {h, 0u, 0u, 0u};
+        append(__activemask(), key_of(h) >= bound ? 1u : 0u, w, i);
+      };
+      if (v) {
+        // only threads whose maximum reaches the bound hold logits >= bound: the
+        // block re-reads just their vectors (thread t read t + kThreads * m)
+        if (mx >= bound) s_list[atomicAdd(&s_na, 1)] = tid;
+        __syncthreads();
+        const int64_t nv = n / 8;
+        const int per = (int)((nv + kThreads - 1) / kThreads);
+        const int total = s_na * per;
+        const uint4 *rv = reinterpret_cast<const uint4 *>(row);
+        for (int w0 = tid; w0 < total; w0 += kThreads * 4) {
+          uint4 qv[4];
+          int64_t iv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int w = w0 + u * kThreads;
+            iv[u] = -1;
+            if (w < total) {
+              const int a = w / per;
+              const int64_t i = s_list[a] + (int64_t)(w - a * per) * kThreads;
+              if (i < nv) {
+                iv[u] = i;
+                qv[u] = ldg_policy(rv + i, drop);
               }
-              append(act, pend, w, i0);
             }
-          },
-          [&](int64_t i, uint32_t h) {
-            const uint32_t w[4] = {h, 0u, 0u, 0u};
-            append(__activemask(), key_of(h) >= bound ? 1u : 0u, w, i);
-          });
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            if (iv[u] >= 0) screen8(iv[u] * 8, qv[u]);
+        }
+        for (int64_t i = nv * 8 + tid; i < n; i += kThreads) screen1(i, (uint32_t)__ldg(row + i));
+      } else {
+        for_each8(row, n, v, drop, screen8, screen1);
+      }
       __syncthreads();
       const int cnt = s_cnt;
+      if (cnt <= kThreads) {  // uniform; candidates are distinct: rank = number larger
+        if (tid < cnt) {
+          const unsigned long long mine = cand[tid];
+          int rank = 0;
+#pragma unroll 4
+          for (int j = 0; j < cnt; ++j) rank += cand[j] > mine ? 1 : 0;
+          if (rank < k) {
+            const int64_t o = orow * k + rank;
+            out_idx[o] = (int32_t)(0xFFFFFFFFu - (uint32_t)(mine & 0xFFFFFFFFull) + off);
+            out_val[o] = half_bits_of((uint32_t)(mine >> 32));
+          }
+        }
+        return;
+      }
       if (cnt <= kCap) {  // uniform
         int mc = 1;
         while (mc < cnt) mc <<= 1;
