@@ -12,8 +12,8 @@
 // Design (HBM-bound: one read of the row from DRAM, a partial second from L2), one CTA
 // per row, on an order-preserving 16-bit key of the fp16 bits:
 //   * fast path (k <= 512): every thread takes the max of its slice (fp16 max
-//     over 16-byte vectors); the k-th largest of those maxima -- found by a
-//     binary search over the key bits with block-wide counts -- is a lower
+//     over 16-byte vectors); the k-th largest of those maxima -- found from
+//     256-bin shared-memory histograms of their high, then low byte -- is a lower
 //     bound of the row's k-th largest key (the k maxima above it are k
 //     distinct logits), so the logits at or above it contain the answer, ties
 //     included.  Only the ~k threads whose maximum reaches the bound can hold
@@ -218,6 +218,35 @@ VA_DEVINL int radix_step(const uint16_t *row, int64_t n, bool vec, int shift, ui
   return total;
 }
 
+// Warp 0: the bin b of hist[256] holding the r-th largest entry (1-based,
+// counting from bin 255 down): *bin = b (-1 when the total is below r),
+// *above = the count in bins above b.
+VA_DEVINL void find_bin(const int *hist, int r, int *bin, int *above) {
+  const int lane = threadIdx.x & 31;
+  int c[8], s = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    c[j] = hist[255 - 8 * lane - j];
+    s += c[j];
+  }
+  int incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  int run = incl - s;
+  if (lane == 31 && incl < r) *bin = -1;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (run < r && run + c[j] >= r) {
+      *bin = 255 - 8 * lane - j;
+      *above = run;
+    }
+    run += c[j];
+  }
+}
+
 // Grid (rows, slices): CTA (r, c) selects the top k of logits [c * slice, (c+1) * slice)
 // of row r (the whole row when there is one slice) into output row r * slices + c,
 // indices relative to the row.
@@ -239,6 +268,8 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
   const uint16_t *row = logits + (int64_t)blockIdx.x * row_stride + off;
   const bool v = vec != 0;
   const int64_t orow = (int64_t)blockIdx.x * gridDim.y + blockIdx.y;
+  if (k <= kThreads)
+    for (int i = tid; i < 512; i += kThreads) (&whist[0][0])[i] = 0;
 
   // ---- fast path: bound from the per-thread maxima, screen, sort ----
   if (k <= kThreads) {
@@ -262,12 +293,21 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
       s_cnt = 0;
       s_na = 0;
     }
-    // the k-th largest thread max = the largest x with #(maxima >= x) >= k
+    // the k-th largest thread max (0 when fewer than k are valid): 256-bin
+    // histograms of the maxima's high byte, then of the low bytes in its bin
+    __syncthreads();  // the histograms' zeroing is complete
+    if (mx != 0u) atomicAdd(&whist[0][mx >> 8], 1);
+    __syncthreads();
+    if (tid < 32) find_bin(whist[0], k, &s_bin, &s_above);
+    __syncthreads();
+    const int hb = s_bin;
     uint32_t bound = 0;
-#pragma unroll 1
-    for (int bit = 15; bit >= 0; --bit) {
-      const uint32_t x = bound | (1u << bit);
-      if (__syncthreads_count(mx >= x) >= k) bound = x;
+    if (hb >= 0) {  // uniform
+      if ((int)(mx >> 8) == hb) atomicAdd(&whist[1][mx & 0xFFu], 1);
+      __syncthreads();
+      if (tid < 32) find_bin(whist[1], k - s_above, &s_gt, &s_ties);
+      __syncthreads();
+      bound = ((uint32_t)hb << 8) | (uint32_t)s_gt;
     }
     if (bound != 0u) {  // at least k valid logits: the answer is inside the bound
       // screen 8 at a time against the bound's value (a superset of the keys >=
