@@ -9,21 +9,21 @@
 // -inf.  Ties are resolved by the lower index (the reference's order between
 // equal values depends on its thread layout; values are identical either way).
 //
-// Design (HBM-bound: one read of the row from DRAM, a partial second from L2), one CTA
+// Design (HBM-bound: one read of the row from DRAM, ~3 % of it read again), one CTA
 // per row, on an order-preserving 16-bit key of the fp16 bits:
-//   * fast path (k <= 512): every thread takes the max of its slice (fp16 max
-//     over 16-byte vectors); the k-th largest of those maxima -- found from
+//   * fast path (k <= 512): every thread takes the maxima of 4 sub-regions of
+//     its slice (fp16 max over 16-byte vectors); the k-th largest of those maxima -- found from
 //     256-bin shared-memory histograms of their high, then low byte -- is a lower
 //     bound of the row's k-th largest key (the k maxima above it are k
 //     distinct logits), so the logits at or above it contain the answer, ties
-//     included.  Only the ~k threads whose maximum reaches the bound can hold
-//     such logits: a second pass re-reads just their vectors (from L2), 8
+//     included.  Only the ~k sub-regions whose maximum reaches the bound can
+//     hold such logits: a second pass re-reads just their vectors, 8
 //     logits at a time with an fp16 compare against the bound, and appends the
 //     few that pass to shared memory (warp-aggregated slots).  Each candidate's
 //     rank in (key desc, index asc) order is the count of larger candidates
 //     (one thread per candidate; a bitonic sort for long lists), and the first
 //     k are written at their ranks.
-//   * exact path (k > 512, fewer than k threads holding a valid logit, or more
+//   * exact path (k > 512, fewer than k valid sub-region maxima, or more
 //     than kCap logits passing the bound, e.g. a row of equal logits): a radix
 //     select -- 256-bin histograms of the high, then the low byte (per-warp
 //     private bins) -- finds the exact k-th key; the keys above it (any order)
@@ -260,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
   __shared__ int s_bin, s_above, s_gt, s_ties;
   __shared__ unsigned long long cand[kCap];
   __shared__ int s_cnt, s_na;
-  __shared__ int s_list[kThreads];  // threads whose maximum reaches the bound
+  __shared__ int s_list[4 * kThreads];  // sub-regions whose maximum reaches the bound
   va::pdl_enter();
   const int tid = threadIdx.x, lane = tid & 31;
   const int64_t off = (int64_t)blockIdx.y * slice;  // a multiple of 8 (host)
@@ -273,29 +273,49 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
 
   // ---- fast path: bound from the per-thread maxima, screen, sort ----
   if (k <= kThreads) {
-    // fp16 max of the vectors (NaN ignored; whether -0 or +0 wins a tie only
-    // lowers the bound, which stays valid), keys for the rest
+    // Maxima of 4 sub-regions per thread (sub-region u: vectors tid + u * kThreads
+    // + m * 4 * kThreads; fp16 max, NaN ignored; whether -0 or +0 wins a tie only
+    // lowers the bound, which stays valid) and of the scalar logits (the tail of a
+    // vectorised row, every logit of an unaligned one).
+    uint32_t sm[4] = {0u, 0u, 0u, 0u};
     uint32_t mx = 0;
-    __half2 m2 = as_h2(0xFC00FC00u);  // (-inf, -inf)
     // the first read keeps the row in L2 for the second (evict_last), which
     // releases it (evict_first)
     uint64_t keep, drop;
     asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(keep));
     asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(drop));
-    for_each8(
-        row, n, v, keep,
-        [&](int64_t, const uint4 &q) {
-          m2 = __hmax2(m2, __hmax2(__hmax2(as_h2(q.x), as_h2(q.y)), __hmax2(as_h2(q.z), as_h2(q.w))));
-        },
-        [&](int64_t, uint32_t h) { mx = max(mx, key_of(h)); });
-    mx = max(mx, max(key_of(as_u32(m2) & 0xFFFFu), key_of(as_u32(m2) >> 16)));
+    const int64_t nv = v ? n / 8 : 0;
+    {
+      const uint4 *rv = reinterpret_cast<const uint4 *>(row);
+      __half2 m2[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) m2[u] = as_h2(0xFC00FC00u);  // (-inf, -inf)
+      for (int64_t i0 = tid; i0 < nv; i0 += (int64_t)kThreads * 4) {
+        uint4 q[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i0 + u * kThreads < nv) q[u] = ldg_policy(rv + i0 + u * kThreads, keep);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (i0 + u * kThreads < nv)
+            m2[u] = __hmax2(m2[u], __hmax2(__hmax2(as_h2(q[u].x), as_h2(q[u].y)),
+                                           __hmax2(as_h2(q[u].z), as_h2(q[u].w))));
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        sm[u] = max(key_of(as_u32(m2[u]) & 0xFFFFu), key_of(as_u32(m2[u]) >> 16));
+    }
+    for (int64_t i = nv * 8 + tid; i < n; i += kThreads) mx = max(mx, key_of(__ldg(row + i)));
     if (tid == 0) {
       s_cnt = 0;
       s_na = 0;
     }
-    // the k-th largest thread max (0 when fewer than k are valid): 256-bin
-    // histograms of the maxima's high byte, then of the low bytes in its bin
+    // the k-th largest of these maxima (0 when fewer than k are valid): 256-bin
+    // histograms of their high byte, then of the low bytes in its bin
     __syncthreads();  // the histograms' zeroing is complete
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (sm[u] != 0u) atomicAdd(&whist[0][sm[u] >> 8], 1);
     if (mx != 0u) atomicAdd(&whist[0][mx >> 8], 1);
     __syncthreads();
     if (tid < 32) find_bin(whist[0], k, &s_bin, &s_above);
@@ -303,7 +323,10 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
     const int hb = s_bin;
     uint32_t bound = 0;
     if (hb >= 0) {  // uniform
-      if ((int)(mx >> 8) == hb) atomicAdd(&whist[1][mx & 0xFFu], 1);
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (sm[u] != 0u && (int)(sm[u] >> 8) == hb) atomicAdd(&whist[1][sm[u] & 0xFFu], 1);
+      if (mx != 0u && (int)(mx >> 8) == hb) atomicAdd(&whist[1][mx & 0xFFu], 1);
       __syncthreads();
       if (tid < 32) find_bin(whist[1], k - s_above, &s_gt, &s_ties);
       __syncthreads();
@@ -350,12 +373,14 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
         append(__activemask(), key_of(h) >= bound ? 1u : 0u, w, i);
       };
       if (v) {
-        // only threads whose maximum reaches the bound hold logits >= bound: the
-        // block re-reads just their vectors (thread t read t + kThreads * m)
-        if (mx >= bound) s_list[atomicAdd(&s_na, 1)] = tid;
+        // only sub-regions whose maximum reaches the bound hold vector logits >=
+        // bound: the block re-reads just those; the scalar tail is screened whole
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (sm[u] >= bound) s_list[atomicAdd(&s_na, 1)] = tid + u * kThreads;
         __syncthreads();
-        const int64_t nv = n / 8;
-        const int per = (int)((nv + kThreads - 1) / kThreads);
+        const int64_t stride = (int64_t)kThreads * 4;
+        const int per = (int)((nv + stride - 1) / stride);
         const int total = s_na * per;
         const uint4 *rv = reinterpret_cast<const uint4 *>(row);
         for (int w0 = tid; w0 < total; w0 += kThreads * 4) {
@@ -367,7 +392,7 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
             iv[u] = -1;
             if (w < total) {
               const int a = w / per;
-              const int64_t i = s_list[a] + (int64_t)(w - a * per) * kThreads;
+              const int64_t i = s_list[a] + (int64_t)(w - a * per) * stride;
               if (i < nv) {
                 iv[u] = i;
                 qv[u] = ldg_policy(rv + i, drop);
