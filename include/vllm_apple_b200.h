@@ -299,9 +299,9 @@ VA_API int va_silu_mul(void *out, const void *gate, const void *up, int64_t num_
 VA_API int va_topk(int32_t *indices, void *values, const void *logits, int64_t num_tokens,
                    int64_t vocab_size, int64_t row_stride, int k, void *stream);
 
-/* The same selection with a caller workspace: when there are fewer rows than SMs, each
- * row is split into slices selected by separate CTAs and merged (same results).
- * va_topk_workspace_size returns the bytes needed (0: no split, any workspace works). */
+/* The same selection with a caller workspace (kept for callers that pass one): every
+ * row is selected whole by one CTA, so va_topk_workspace_size returns 0 and any
+ * workspace (also none) works; results equal va_topk's. */
 VA_API size_t va_topk_workspace_size(int64_t num_tokens, int64_t vocab_size, int k);
 VA_API int va_topk_ws(int32_t *indices, void *values, const void *logits, int64_t num_tokens,
                       int64_t vocab_size, int64_t row_stride, int k, void *workspace,

@@ -99,13 +99,24 @@ def test_topk_rejects():
 @pytest.mark.parametrize("T,V,k", [(1, 151936, 50), (8, 131072, 50), (16, 32000, 8),
                                    (40, 131072, 256), (3, 4100, 20), (64, 262144, 100)])
 @pytest.mark.parametrize("special", [False, True])
-def test_topk_split_rows(T, V, k, special):
-    """Few rows: slices of a row on separate CTAs, then a merge; same results."""
+def test_topk_few_rows(T, V, k, special):
+    """Few rows (a decode batch): one CTA per whole row, no workspace; through the
+    workspace entry point with a workspace given anyway, the same results."""
     from vllm_apple_b200 import _lib
     lib = _lib.load()
-    if T < 148 and V >= 8192:
-        assert lib.va_topk_workspace_size(T, V, k) > 0  # the split path is taken
-    _check(_logits(T * 11 + V + k, T, V, special), k)
+    assert lib.va_topk_workspace_size(T, V, k) == 0
+    x = _logits(T * 11 + V + k, T, V, special)
+    _check(x, k)
+    dx = x.cuda()
+    idx = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    val = torch.empty(T, k, dtype=torch.float16, device="cuda")
+    junk = torch.empty(1 << 20, dtype=torch.uint8, device="cuda")
+    _lib.check(lib.va_topk_ws(idx.data_ptr(), val.data_ptr(), dx.data_ptr(), T, V, V, k,
+                              junk.data_ptr(), junk.numel(),
+                              torch.cuda.current_stream().cuda_stream), "va_topk_ws")
+    ei, ev = ref.topk(x.numpy(), k)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ei)
+    np.testing.assert_array_equal(val.cpu().view(torch.int16).numpy(), ev.view(np.int16))
 
 
 @pytest.mark.parametrize("T,V,k", [(32, 32000, 50), (4, 151936, 256), (1024, 131072, 50)])

@@ -247,13 +247,10 @@ VA_DEVINL void find_bin(const int *hist, int r, int *bin, int *above) {
   }
 }
 
-// Grid (rows, slices): CTA (r, c) selects the top k of logits [c * slice, (c+1) * slice)
-// of row r (the whole row when there is one slice) into output row r * slices + c,
-// indices relative to the row.
+// One CTA per row: CTA r selects the top k of row r into output row r.
 __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uint16_t *out_val,
                                                         const uint16_t *logits, int64_t n_row,
-                                                        int64_t row_stride, int k, int vec,
-                                                        int64_t slice) {
+                                                        int64_t row_stride, int k, int vec) {
   __shared__ int whist[kWarps][256];
   __shared__ int hist[256];
   __shared__ int warp_sums[kWarps];
@@ -263,11 +260,11 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
   __shared__ int s_list[4 * kThreads];  // sub-regions whose maximum reaches the bound
   va::pdl_enter();
   const int tid = threadIdx.x, lane = tid & 31;
-  const int64_t off = (int64_t)blockIdx.y * slice;  // a multiple of 8 (host)
-  const int64_t n = n_row - off < slice ? (n_row - off > 0 ? n_row - off : 0) : slice;
-  const uint16_t *row = logits + (int64_t)blockIdx.x * row_stride + off;
+  constexpr int64_t off = 0;  // indices are relative to the row
+  const int64_t n = n_row;
+  const uint16_t *row = logits + (int64_t)blockIdx.x * row_stride;
   const bool v = vec != 0;
-  const int64_t orow = (int64_t)blockIdx.x * gridDim.y + blockIdx.y;
+  const int64_t orow = blockIdx.x;
   if (k <= kThreads)
     for (int i = tid; i < 512; i += kThreads) (&whist[0][0])[i] = 0;
 
@@ -527,97 +524,17 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
   }
 }
 
-// Merge of the per-slice lists: row r's slices * k (index, value) candidates
-// (index -1 = padding), ordered by (key desc, index asc), the first k written.
-constexpr int kMergeCap = 4096;
-__global__ void __launch_bounds__(kThreads) topk_merge_kernel(int32_t *out_idx, uint16_t *out_val,
-                                                              const int32_t *ws_idx,
-                                                              const uint16_t *ws_val, int slices,
-                                                              int k) {
-  __shared__ unsigned long long cand[kMergeCap];
-  va::pdl_enter();
-  const int tid = threadIdx.x;
-  const int nc = slices * k;
-  int m = 1;
-  while (m < nc) m <<= 1;
-  const int64_t base = (int64_t)blockIdx.x * nc;
-  for (int i = tid; i < m; i += kThreads) {
-    unsigned long long c = 0ull;
-    if (i < nc) {
-      const int32_t idx = ws_idx[base + i];
-      if (idx >= 0) c = pack_cand(key_of(ws_val[base + i]), idx);
-    }
-    cand[i] = c;
-  }
-  __syncthreads();
-  sort_desc<false>(cand, m);
-  for (int i = tid; i < k; i += kThreads) {
-    const unsigned long long c = cand[i];
-    const int64_t o = (int64_t)blockIdx.x * k + i;
-    if (c == 0ull) {
-      out_idx[o] = -1;
-      out_val[o] = 0xFC00u;
-    } else {
-      out_idx[o] = (int32_t)(0xFFFFFFFFu - (uint32_t)(c & 0xFFFFFFFFull));
-      out_val[o] = half_bits_of((uint32_t)(c >> 32));
-    }
-  }
-}
-
-// Slices per row: with fewer rows than SMs, a row is split so that about two CTAs
-// per SM are busy; slices of at least 4096 logits, a merge list of <= kMergeCap.
-int topk_slices(int64_t T, int64_t V, int k) {
-  const int64_t sms = va_host::sm_count();
-  if (T <= 0 || T >= sms || k > kThreads) return 1;
-  int64_t c = (2 * sms + T - 1) / T;
-  if (c > 16) c = 16;
-  if (c > V / 4096) c = V / 4096;
-  if (c * k > kMergeCap) c = kMergeCap / k;
-  return c < 2 ? 1 : (int)c;
-}
-
-int64_t topk_slice_len(int64_t V, int c) { return ((V + c - 1) / c + 7) / 8 * 8; }
-
 }  // namespace
 
-extern "C" size_t va_topk_workspace_size(int64_t num_tokens, int64_t vocab_size, int k) {
-  if (num_tokens <= 0 || vocab_size <= 0 || k < 1 || k > kMaxK) return 0;
-  const int c = topk_slices(num_tokens, vocab_size, k);
-  if (c < 2) return 0;
-  const size_t n = (size_t)num_tokens * c * k;
-  return ((n * 4 + 255) / 256) * 256 + n * 2;
-}
+// Every row runs whole on one CTA: cutting the rows of small batches into slices
+// on separate CTAs plus a merge kernel measured 2-3x slower under graph replay
+// (8 x 131072: 17.8 us against 7.0), so no workspace is needed.
+extern "C" size_t va_topk_workspace_size(int64_t, int64_t, int) { return 0; }
 
 extern "C" int va_topk_ws(int32_t *indices, void *values, const void *logits,
                           int64_t num_tokens, int64_t vocab_size, int64_t row_stride, int k,
-                          void *workspace, size_t workspace_bytes, void *stream) {
-  if (num_tokens < 0 || vocab_size < 0 || k < 1 || row_stride < vocab_size)
-    return VA_ERR_INVALID_ARG;
-  if (k > kMaxK || vocab_size > INT32_MAX - 1 || num_tokens > INT32_MAX) return VA_ERR_UNSUPPORTED;
-  if (num_tokens == 0) return VA_OK;
-  if (!indices || !values || !logits) return VA_ERR_INVALID_ARG;
-  const int c = topk_slices(num_tokens, vocab_size, k);
-  const int vec = (va_host::aligned16(logits) && row_stride % 8 == 0) ? 1 : 0;
-  auto st = static_cast<cudaStream_t>(stream);
-  if (c < 2 || !vec) {  // one CTA per row
-    va_host::launch_pdl(topk_kernel, dim3((unsigned)num_tokens, 1), kThreads, st,
-        indices, static_cast<uint16_t *>(values), static_cast<const uint16_t *>(logits),
-        vocab_size, row_stride, k, vec, vocab_size);
-    return va_host::launch_status();
-  }
-  if (!workspace || workspace_bytes < va_topk_workspace_size(num_tokens, vocab_size, k))
-    return VA_ERR_WORKSPACE;
-  const size_t n = (size_t)num_tokens * c * k;
-  int32_t *ws_idx = static_cast<int32_t *>(workspace);
-  uint16_t *ws_val = reinterpret_cast<uint16_t *>(static_cast<unsigned char *>(workspace) +
-                                                  ((n * 4 + 255) / 256) * 256);
-  va_host::launch_pdl(topk_kernel, dim3((unsigned)num_tokens, (unsigned)c), kThreads, st,
-      ws_idx, ws_val, static_cast<const uint16_t *>(logits), vocab_size, row_stride, k, vec,
-      topk_slice_len(vocab_size, c));
-  if (va_host::launch_status() != VA_OK) return VA_ERR_LAUNCH;
-  va_host::launch_pdl(topk_merge_kernel, (unsigned)num_tokens, kThreads, st,
-      indices, static_cast<uint16_t *>(values), ws_idx, ws_val, c, k);
-  return va_host::launch_status();
+                          void *, size_t, void *stream) {
+  return va_topk(indices, values, logits, num_tokens, vocab_size, row_stride, k, stream);
 }
 
 extern "C" int va_topk(int32_t *indices, void *values, const void *logits, int64_t num_tokens,
@@ -628,8 +545,8 @@ extern "C" int va_topk(int32_t *indices, void *values, const void *logits, int64
   if (num_tokens == 0) return VA_OK;
   if (!indices || !values || !logits) return VA_ERR_INVALID_ARG;
   const int vec = (va_host::aligned16(logits) && row_stride % 8 == 0) ? 1 : 0;
-  va_host::launch_pdl(topk_kernel, dim3((unsigned)num_tokens, 1), kThreads,
-                      static_cast<cudaStream_t>(stream), indices, static_cast<uint16_t *>(values), static_cast<const uint16_t *>(logits),
-      vocab_size, row_stride, k, vec, vocab_size);
+  va_host::launch_pdl(topk_kernel, (unsigned)num_tokens, kThreads,
+                      static_cast<cudaStream_t>(stream), indices, static_cast<uint16_t *>(values),
+                      static_cast<const uint16_t *>(logits), vocab_size, row_stride, k, vec);
   return va_host::launch_status();
 }
