@@ -260,11 +260,10 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
   __shared__ int s_list[4 * kThreads];  // sub-regions whose maximum reaches the bound
   va::pdl_enter();
   const int tid = threadIdx.x, lane = tid & 31;
-  constexpr int64_t off = 0;  // indices are relative to the row
   const int64_t n = n_row;
   const uint16_t *row = logits + (int64_t)blockIdx.x * row_stride;
   const bool v = vec != 0;
-  const int64_t orow = blockIdx.x;
+  const int64_t orow = blockIdx.x;  // output row
   if (k <= kThreads)
     for (int i = tid; i < 512; i += kThreads) (&whist[0][0])[i] = 0;
 
@@ -414,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
           for (int j = 0; j < cnt; ++j) rank += cand[j] > mine ? 1 : 0;
           if (rank < k) {
             const int64_t o = orow * k + rank;
-            out_idx[o] = (int32_t)(0xFFFFFFFFu - (uint32_t)(mine & 0xFFFFFFFFull) + off);
+            out_idx[o] = (int32_t)(0xFFFFFFFFu - (uint32_t)(mine & 0xFFFFFFFFull));
             out_val[o] = half_bits_of((uint32_t)(mine >> 32));
           }
         }
@@ -434,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
         for (int i = tid; i < k; i += kThreads) {
           const unsigned long long c = cand[i];
           const int64_t o = orow * k + i;
-          out_idx[o] = (int32_t)(0xFFFFFFFFu - (uint32_t)(c & 0xFFFFFFFFull) + off);
+          out_idx[o] = (int32_t)(0xFFFFFFFFu - (uint32_t)(c & 0xFFFFFFFFull));
           out_val[o] = half_bits_of((uint32_t)(c >> 32));
         }
         return;
@@ -518,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 3) topk_kernel(int32_t *out_idx, uin
       out_idx[o] = -1;
       out_val[o] = 0xFC00u;  // -inf
     } else {
-      out_idx[o] = (int32_t)(0xFFFFFFFFu - (uint32_t)(c & 0xFFFFFFFFull) + off);
+      out_idx[o] = (int32_t)(0xFFFFFFFFu - (uint32_t)(c & 0xFFFFFFFFull));
       out_val[o] = half_bits_of((uint32_t)(c >> 32));
     }
   }
