@@ -174,3 +174,22 @@ def test_topk_many_rows_edge_rows(V):
     ei, ev = ref.topk(xs.numpy(), k)
     np.testing.assert_array_equal(idx.cpu().numpy(), ei)
     np.testing.assert_array_equal(val.cpu().view(torch.int16).numpy(), ev.view(np.int16))
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_topk_random_tie_heavy(seed):
+    """Seeded random shapes (V not a multiple of 8, odd row strides, k up to 512 and
+    beyond) over logits drawn from a small set of values, so that ties at the bound,
+    candidate lists longer than k and overflows into the exact path all occur; bit
+    for bit against the oracle."""
+    g = torch.Generator().manual_seed(1234 + seed)
+    for _ in range(4):
+        T = int(torch.randint(1, 300, (1,), generator=g))
+        V = int(torch.randint(9, 40000, (1,), generator=g))
+        k = int(torch.randint(1, 600, (1,), generator=g))
+        levels = int(torch.randint(2, 200, (1,), generator=g))
+        x = (torch.randint(0, levels, (T, V), generator=g).float() / 7 - 3).half()
+        if seed % 2:
+            x[:, torch.randint(0, V, (V // 50 + 1,), generator=g)] = float("nan")
+        stride = None if seed % 3 else V + int(torch.randint(0, 16, (1,), generator=g))
+        _check(x, k, stride=stride)
