@@ -309,32 +309,39 @@ class MetalAttentionImpl(AttentionImpl):
         token see its whole sequence."""
         T = md.num_actual_tokens
         bs = 16
-        qsl = md.query_start_loc_cpu
-        S = len(qsl) - 1
-        lens = [qsl[s + 1] - qsl[s] for s in range(S)]
-        nblk = [(n + bs - 1) // bs for n in lens]
-        width = max(max(nblk, default=1), 1)
+        bt, slots, tok, pos, total = encoder_layout(md.query_start_loc_cpu, bs)
         dev = q3.device
-        total = max(sum(nblk), 1)
         kc = torch.zeros(total, bs, self.num_kv_heads, self.head_size, dtype=torch.float16,
                          device=dev)
         vc = torch.zeros_like(kc)
-        bt = torch.full((S, width), -1, dtype=torch.int32)
-        slots, tok, pos, at = [], [], [], 0
-        for s in range(S):
-            bt[s, :nblk[s]] = torch.arange(at, at + nblk[s], dtype=torch.int32)
-            slots += [at * bs + i for i in range(lens[s])]
-            tok += [s] * lens[s]
-            pos += [lens[s] - 1] * lens[s]
-            at += nblk[s]
         k3 = self._kv3(key, T)
         v3 = self._kv3(value, T)
-        ops.kv_write_slots(kc, vc, k3, v3, torch.tensor(slots, dtype=torch.int64, device=dev),
-                           layout="nhd")
-        ops.paged_prefill(o3, q3, kc, vc, bt.to(dev),
-                          torch.tensor(tok, dtype=torch.int32, device=dev),
-                          torch.tensor(pos, dtype=torch.int32, device=dev), scale=self.scale,
+        ops.kv_write_slots(kc, vc, k3, v3, slots.to(dev), layout="nhd")
+        ops.paged_prefill(o3, q3, kc, vc, bt.to(dev), tok.to(dev), pos.to(dev), scale=self.scale,
                           layout="nhd")
+
+
+def encoder_layout(query_start_loc, bs: int):
+    """Scratch cache layout of a non-causal (encoder) batch, built with tensor ops:
+    sequence s gets ceil(len_s / bs) consecutive blocks; returns the block table
+    [S, width] int32 (-1 padded), the slot of every token (int64), its sequence
+    (int32), the position every token attends up to (the sequence's last, int32)
+    and the number of blocks (>= 1)."""
+    qsl = torch.as_tensor(query_start_loc, dtype=torch.int64)
+    S = qsl.numel() - 1
+    lens = qsl[1:] - qsl[:-1]
+    nblk = (lens + bs - 1) // bs
+    width = max(int(nblk.max()) if S > 0 else 1, 1)
+    first = torch.cumsum(nblk, 0) - nblk  # first block of each sequence
+    col = torch.arange(width, dtype=torch.int64)
+    bt = torch.where(col[None, :] < nblk[:, None], first[:, None] + col[None, :],
+                     torch.full((), -1, dtype=torch.int64)).to(torch.int32)
+    tok = torch.repeat_interleave(torch.arange(S, dtype=torch.int64), lens)
+    off = torch.arange(tok.numel(), dtype=torch.int64) - qsl[:-1][tok]
+    slots = first[tok] * bs + off
+    pos = (lens - 1)[tok].to(torch.int32)
+    total = max(int(nblk.sum()), 1)
+    return bt, slots, tok.to(torch.int32), pos, total
 
 
 B200AttentionImpl = MetalAttentionImpl
