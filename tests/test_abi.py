@@ -108,3 +108,21 @@ def test_decode_plan_regimes(lib):
     # Qwen shape at 1024 units stays split (and ordered): partials + order
     w = f(512, 14, 2, 64, 16, 4096)
     assert w > 512 * 4 and (w - ((512 * 4 + 255) // 256) * 256) % 256 == 0
+
+
+def test_topk_entry_points_host_side(lib):
+    """Top-k argument checks and the workspace contract, host side only: every row
+    runs whole on one CTA, so no workspace is ever needed; invalid arguments are
+    rejected before any launch and empty batches succeed without one."""
+    P = ctypes.c_void_p
+    for T, V, k in ((1, 131072, 50), (64, 32000, 8), (1024, 151936, 1024), (3, 7, 3)):
+        assert lib.va_topk_workspace_size(T, V, k) == 0
+    # k out of range, row stride below the vocabulary, negative sizes, null buffers
+    assert lib.va_topk(P(16), P(16), P(16), 4, 100, 100, 0, None) == 1
+    assert lib.va_topk(P(16), P(16), P(16), 4, 100, 99, 5, None) == 1
+    assert lib.va_topk(P(16), P(16), P(16), -1, 100, 100, 5, None) == 1
+    assert lib.va_topk(None, None, None, 4, 100, 100, 5, None) == 1
+    assert lib.va_topk(P(16), P(16), P(16), 4, 100, 100, 1025, None) == 2
+    assert lib.va_topk_ws(None, None, None, 4, 100, 100, 5, None, 0, None) == 1
+    assert lib.va_topk(None, None, None, 0, 100, 100, 5, None) == 0
+    assert lib.va_topk_ws(None, None, None, 0, 100, 100, 5, None, 0, None) == 0
