@@ -12,17 +12,17 @@
 // Design (HBM-bound: one read of the row from DRAM, ~3 % of it read again), one CTA
 // per row, on an order-preserving 16-bit key of the fp16 bits:
 //   * fast path (k <= 512): every thread takes the maxima of 4 sub-regions of
-//     its slice (fp16 max over 16-byte vectors); the k-th largest of those maxima -- found from
-//     256-bin shared-memory histograms of their high, then low byte -- is a lower
-//     bound of the row's k-th largest key (the k maxima above it are k
-//     distinct logits), so the logits at or above it contain the answer, ties
-//     included.  Only the ~k sub-regions whose maximum reaches the bound can
-//     hold such logits: a second pass re-reads just their vectors, 8
-//     logits at a time with an fp16 compare against the bound, and appends the
-//     few that pass to shared memory (warp-aggregated slots).  Each candidate's
-//     rank in (key desc, index asc) order is the count of larger candidates
-//     (one thread per candidate; a bitonic sort for long lists), and the first
-//     k are written at their ranks.
+//     its share of the row (fp16 max over 16-byte vectors); the k-th largest of
+//     those maxima -- found from 256-bin shared-memory histograms of their high,
+//     then low byte -- is a lower bound of the row's k-th largest key (the k
+//     maxima above it are k distinct logits), so the logits at or above it
+//     contain the answer, ties included.  Only the ~k sub-regions whose maximum
+//     reaches the bound can hold such logits: a second pass re-reads just their
+//     vectors, 8 logits at a time with an fp16 compare against the bound, and
+//     appends the few that pass to shared memory (warp-aggregated slots).  Each
+//     candidate's rank in (key desc, index asc) order is the count of larger
+//     candidates (one thread per candidate; a bitonic sort for long lists), and
+//     the first k are written at their ranks.
 //   * exact path (k > 512, fewer than k valid sub-region maxima, or more
 //     than kCap logits passing the bound, e.g. a row of equal logits): a radix
 //     select -- 256-bin histograms of the high, then the low byte (per-warp
